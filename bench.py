@@ -1,0 +1,447 @@
+"""Benchmark of the DVAttn paged decode on B200 (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Default workload: BASELINE config 2 (bf16 batched paged decode, W=32, 64/4 heads, E=128,
+R=64, KV lengths U[512, 8192] in two turns, page 16).  A step is one call of the op over
+one batch (one layer-step).  Metric: algorithmic HBM GB/s of the op (attended K/V rows +
+q + out + cos/sin + tables), and microseconds per layer-step.
+
+* value: device-resident inputs, K calls of the C ABI (libdvattn_b200.so) timed with CUDA
+  events on the launching stream; between steps the call rotates over three copies of
+  the KV page pool (each larger than the 126 MB L2), so no step reads K/V from L2 left by
+  the previous one.
+* e2e: the same metric through the public torch op (torch.ops.libdvatt.dvattn_paged_sdpa)
+  with the step's inputs (q, cos/sin, locations, fragment lengths, block tables) copied
+  from pinned host memory and the output copied back inside the timed region; the KV
+  cache stays resident, as in a serving engine.
+* roofline: the attention kernel alone (C-ABI phase ATTEND between CUDA events), against
+  the measured HBM copy bandwidth of MEASURED_PEAKS.json.
+* cpu_baseline: the reference's pure-PyTorch path (oracle restatement of
+  dvattn_sdpa_pt + apply_rotary_pos_emb) on a bounded sample, on rank 0 only.
+* Multi-GPU (torchrun): weak scaling -- every rank decodes its own batch of the same
+  shape, no collective on the data path; value = all ranks' bytes / max-over-ranks time.
+  --workload long3: config 3 KV-chunk-sharded across ranks + NCCL all-gather LSE merge.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode attn HBM GB/s (% of peak) and µs/layer-step at 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def traffic_from_profiles(workload: str):
+    """DRAM bytes per launch of the attention kernel from the committed ncu summary
+    (profiles/traffic.txt: `<workload> <kernel> <bytes_per_launch>` lines), or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        parts = line.split()
+        if len(parts) >= 3 and parts[0] == workload and not line.startswith("#"):
+            try:
+                return int(float(parts[2]))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------
+# CPU baseline: the reference's pure-PyTorch path on a bounded sample
+# ------------------------------------------------------------------------------------
+def cpu_sample_gbs(case_fn, n_seq: int, reps: int = 3):
+    """Time oracle.paged_via_sdpa_pt (dvattn_sdpa_pt + apply_rotary_pos_emb restated) on the
+    first n_seq sequences of the workload; returns (GB/s, threads, description)."""
+    from oracle import dvattn_oracle as O
+    from dvattn_b200 import workloads as wl
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    c = case_fn(n_seq)
+    args = (c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
+            c.block_tables)
+    O.paged_via_sdpa_pt(*args)  # warm-up (also the page gather)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.paged_via_sdpa_pt(*args)
+        ts.append(time.perf_counter() - t0)
+    t = statistics.median(ts)
+    return wl.paged_bytes(c) / t / 1e9, threads, t
+
+
+# ------------------------------------------------------------------------------------
+# workloads
+# ------------------------------------------------------------------------------------
+def workload_case(name: str, device: str, rank: int = 0, world: int = 1):
+    from dvattn_b200 import workloads as wl
+    if name == "config2":
+        return wl.config2(device=device), "config2: bf16 batched paged decode W=32 Hq=64 Hkv=4 E=128 R=64 BS=16 2 turns"
+    if name == "config1":
+        return wl.config1(device=device), "config1: fp32 W=1 Hq=16 Hkv=1 E=128 R=64 L=1024 BS=16"
+    if name == "config3":
+        return wl.config3(device=device), "config3: fp16 long context W=4 Hq=128 Hkv=8 E=128 R=128 L=131072 BS=64"
+    if name == "config5":
+        return wl.config5(device=device), "config5: fp16 serving mix W=256 Hq=32 Hkv=2 E=256 R=64 BS=64 1-4 turns"
+    raise SystemExit(f"unknown workload {name}")
+
+
+def cpu_case_fn(name: str):
+    from dvattn_b200 import workloads as wl
+    if name == "config2":
+        return lambda n: wl.make_paged(wl.config2_lengths(2, 32)[:n], Hq=64, Hkv=4, E=128, R=64, BS=16,
+                                       dtype=torch.bfloat16, seed=2)
+    if name == "config1":
+        return lambda n: wl.config1()
+    if name in ("config3", "long3"):
+        return lambda n: wl.make_paged([[131072 // 16]], Hq=128, Hkv=8, E=128, R=128, BS=64, dtype=torch.float16,
+                                       seed=3)
+    if name == "config5":
+        return lambda n: wl.make_paged(wl.config5_lengths(5, 256)[:n], Hq=32, Hkv=2, E=256, R=64, BS=64,
+                                       dtype=torch.float16, seed=5)
+    raise SystemExit(name)
+
+
+CPU_SAMPLE = {"config2": (4, "first 4 of the 32 sequences of config 2"),
+              "config1": (1, "config 1 whole"),
+              "config3": (1, "1 sequence of 8192 keys (1/16 of one config-3 sequence), 128/8 heads"),
+              "long3": (1, "1 sequence of 8192 keys (1/16 of one config-3 sequence), 128/8 heads"),
+              "config5": (24, "first 24 of the 256 sequences of config 5")}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's own CPU implementation of the path (its
+    pure-PyTorch dvattn_sdpa_pt, restated in oracle/) on the host cores."""
+    if rank != 0:
+        return
+    name = "config3" if args.workload == "long3" else args.workload
+    n, desc = CPU_SAMPLE[name]
+    fn = cpu_case_fn(name)
+    from dvattn_b200 import workloads as wl
+    from oracle import dvattn_oracle as O
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    c = fn(n)
+    a = (c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
+         c.block_tables)
+    for _ in range(args.warmup):
+        O.paged_via_sdpa_pt(*a)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.paged_via_sdpa_pt(*a)
+        ts.append(time.perf_counter() - t0)
+    t = sum(ts) / len(ts)
+    gbs = wl.paged_bytes(c) / t / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": str(c.dtype).replace("torch.", ""),
+            "data": "synthetic (seeded N(0,1) q/k/v)",
+            "config": {"workload": name, "sample": desc, "cpu_threads": threads},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "gpu_launches": 0}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import dvattn_b200
+    from dvattn_b200 import capi
+    from dvattn_b200 import workloads as wl
+    dev = f"cuda:{local}"
+    hbm_peak, _, peak_kind = load_peaks()
+    case, desc = workload_case(args.workload, dev, rank, world)
+    nbytes = wl.paged_bytes(case)
+    # three KV pools (rotation defeats L2 reuse between steps)
+    pools = [(case.k_cache, case.v_cache)]
+    for i in range(2):
+        pools.append((torch.randn_like(case.k_cache, dtype=torch.float32).to(case.dtype),
+                      torch.randn_like(case.v_cache, dtype=torch.float32).to(case.dtype)))
+    out = case.new_out()
+    calls = []
+    ws = None
+    for kc, vc in pools:
+        call = capi.PagedCall(out, case.scale, case.locations, case.queries, case.cosines, case.sines,
+                              case.fragment_lengths, kc, vc, case.block_tables, workspace=ws)
+        ws = call.workspace
+        calls.append(call)
+    stream = torch.cuda.current_stream()
+    launches_per_step = 3
+
+    # ---- value: device-resident inputs, C-ABI call ----
+    for i in range(args.warmup):
+        calls[i % 3]()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(args.steps):
+        calls[i % 3]()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+
+    # ---- attention kernel alone (roofline), same stream, events between phases ----
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        c = calls[i % 3]
+        c.phase(capi.DVATTN_PHASE_SCHEDULE)
+        kev[i][0].record(stream)
+        c.phase(capi.DVATTN_PHASE_ATTEND)
+        kev[i][1].record(stream)
+        c.phase(capi.DVATTN_PHASE_MERGE)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    k_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
+    k_ms = max_over_ranks(k_ms, world)
+
+    # ---- e2e: public torch op, host (pinned) inputs in, output out ----
+    host_in = [t.cpu().pin_memory() for t in (case.queries, case.cosines, case.sines, case.locations,
+                                              case.fragment_lengths, case.block_tables)]
+    dev_in = [torch.empty_like(t, device=dev) for t in host_in]
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step(i):
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        q, cs, sn, loc, L, bt = dev_in
+        kc, vc = pools[i % 3]
+        torch.ops.libdvatt.dvattn_paged_sdpa(out, case.scale, loc, q, cs, sn, L, kc, vc, bt)
+        host_out.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+
+    total_bytes = sum_over_ranks(float(nbytes), world)
+    value = total_bytes / (t_ms * 1e-3) / 1e9
+    e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9
+    achieved = nbytes / (k_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n, sdesc = CPU_SAMPLE[args.workload]
+        gbs, threads, _ = cpu_sample_gbs(cpu_case_fn(args.workload), n)
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sdesc}
+    if rank == 0:
+        traffic = traffic_from_profiles(args.workload)
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_layer_step": round(t_ms * 1e3, 2),
+            "pct_of_peak_hbm": round(100.0 * value / world / hbm_peak, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": str(case.dtype).replace("torch.", ""),
+            "data": "synthetic (seeded N(0,1) q/k/v, seeded lengths/turns/page permutation)",
+            "config": {"workload": desc, "bytes_per_step_per_gpu": nbytes, "parallelism": f"batch-replica x{world}",
+                       "l2": "inputs larger than L2: 3 rotating KV pools of %.0f MB each" %
+                             ((case.k_cache.numel() + case.v_cache.numel()) * case.k_cache.element_size() / 1e6)},
+            "roofline": {"bound": "hbm", "kernel": "decode_tc_kernel" if case.dtype != torch.float32 else
+                         "decode_f32_kernel", "achieved": round(achieved, 2), "peak": hbm_peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                         "kernel_us": round(k_ms * 1e3, 2), "traffic": traffic},
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "us_per_layer_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_paged_sdpa"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_long3(args, world, rank, local):
+    """Config 3 with its KV split across the ranks (page-aligned chunks) and the partial
+    outputs merged over NCCL (all-gather of f32 O + LSE, then the LSE-merge kernel)."""
+    from dvattn_b200 import capi, dist as ddist
+    from dvattn_b200 import workloads as wl
+    import torch.distributed as tdist
+    dev = f"cuda:{local}"
+    hbm_peak, _, peak_kind = load_peaks()
+    full = wl.config3(device=dev)
+    nbytes_total = wl.paged_bytes(full)
+    sh = ddist.kv_chunk_shard(full, rank, world)
+    out = sh.new_out()
+    lse = torch.empty(out.shape[:3], device=dev)
+    o32 = torch.empty(out.shape, device=dev)
+    call = capi.PagedCall(*sh.op_args(out), lse=lse, out_f32=o32)
+    merged = torch.empty_like(out)
+
+    def step():
+        call()
+        if world > 1:
+            ddist.allgather_merge(o32, lse, merged)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    value = nbytes_total / (t_ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 5),
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "float16",
+                          "data": "synthetic", "config": {"workload": "config3 KV-chunk sharded + NCCL LSE merge",
+                                                          "parallelism": f"kv-chunk x{world}"},
+                          "gpu_launches": args.steps * (3 + (1 if world > 1 else 0))}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config2", choices=["config1", "config2", "config3", "config5", "long3"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    if args.workload == "long3":
+        run_long3(args, world, rank, local)
+    else:
+        run_ours(args, world, rank, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,95 @@
+"""Python wrappers in the style of python/dvattn/attention.py (``dvattn_rope``,
+``rotate_half``, ``apply_rotary_pos_emb`` keep the reference names and arguments,
+attention.py:68-88); the paged ops, which the reference only exposes as
+``torch.ops.libdvatt.*``, get thin wrappers that allocate ``out`` when it is not given.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+_ops = torch.ops.libdvatt
+
+
+def dvattn_paged_sdpa(queries: torch.Tensor, locations: torch.Tensor, cosines: torch.Tensor, sines: torch.Tensor,
+                      fragment_lengths: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      block_tables: torch.Tensor, scale: float, out: Optional[torch.Tensor] = None,
+                      lse: Optional[torch.Tensor] = None, out_f32: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Paged multi-turn decode.  queries [W,Hq,S,E] (unrotated), cos/sin [F,W,S,R] f32,
+    locations [F,W,S] i32, fragment_lengths [F] i32, k/v cache [NB,BS,Hkv,E], block_tables
+    [W,max_blocks] i32 -> out [W,Hq,S,Ev].  ``lse`` ([W,Hq,S] f32, natural log) and
+    ``out_f32`` are optional extra outputs."""
+    if out is None:
+        out = torch.empty(queries.shape[:3] + (v_cache.size(3),), dtype=queries.dtype, device=queries.device)
+    if lse is None and out_f32 is None:
+        _ops.dvattn_paged_sdpa(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache,
+                               block_tables)
+    else:
+        _ops.dvattn_paged_sdpa_ex(out, lse, out_f32, scale, locations, queries, cosines, sines, fragment_lengths,
+                                  k_cache, v_cache, block_tables)
+    return out
+
+
+def dvattn_varlen_paged_sdpa(queries: torch.Tensor, locations: torch.Tensor, cosines: torch.Tensor,
+                             sines: torch.Tensor, fragment_lengths: torch.Tensor, k_cache: torch.Tensor,
+                             v_cache: torch.Tensor, block_tables: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                             cu_seqlens_k: Optional[torch.Tensor], scale: float, out: Optional[torch.Tensor] = None,
+                             lse: Optional[torch.Tensor] = None,
+                             out_f32: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Varlen chunked prefill.  queries [T,Hq,E], cos/sin [F,T,R/2] f32, locations [F,T]
+    i32 (negative = turn skipped), cu_seqlens_q [W+1] i32 -> out [T,Hq,Ev]."""
+    if out is None:
+        out = torch.empty((queries.size(0), queries.size(1), v_cache.size(3)), dtype=queries.dtype,
+                          device=queries.device)
+    if cu_seqlens_k is None:
+        cu_seqlens_k = cu_seqlens_q
+    if lse is None and out_f32 is None:
+        _ops.dvattn_varlen_paged_sdpa(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache,
+                                      v_cache, block_tables, cu_seqlens_q, cu_seqlens_k)
+    else:
+        _ops.dvattn_varlen_paged_sdpa_ex(out, lse, out_f32, scale, locations, queries, cosines, sines,
+                                         fragment_lengths, k_cache, v_cache, block_tables, cu_seqlens_q,
+                                         cu_seqlens_k)
+    return out
+
+
+def dvattn_rope(queries: torch.Tensor, cosines: torch.Tensor, sines: torch.Tensor, out=None) -> torch.Tensor:
+    """Same signature as python/dvattn/attention.py:68-72: out [F,W,Hq,S,E]."""
+    if out is None:
+        out = torch.empty((cosines.size(0),) + tuple(queries.shape), dtype=queries.dtype, device=queries.device)
+    _ops.dvattn_rope(out, queries, cosines, sines)
+    return out
+
+
+def dvattn_varlen_rope(queries: torch.Tensor, cosines: torch.Tensor, sines: torch.Tensor, out=None) -> torch.Tensor:
+    """out [F,T,H,E] from queries [T,H,E] and cos/sin [F,T,R/2]."""
+    if out is None:
+        out = torch.empty((cosines.size(0),) + tuple(queries.shape), dtype=queries.dtype, device=queries.device)
+    _ops.dvattn_varlen_rope(out, queries, cosines, sines)
+    return out
+
+
+def dvattn_lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor, out: torch.Tensor,
+                     lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Merge [parts, ..., Ev] f32 partials with their natural-log LSEs [parts, ...] into out."""
+    _ops.dvattn_lse_merge(out, lse_out, part_out, part_lse)
+    return out
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    """Rotates half the hidden dims of the input (python/dvattn/attention.py:75-79)."""
+    x1 = x[..., : x.shape[-1] // 2]
+    x2 = x[..., x.shape[-1] // 2:]
+    return torch.cat((-x2, x1), dim=-1)
+
+
+def apply_rotary_pos_emb(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, unsqueeze_dim: int = 1) -> torch.Tensor:
+    """Partial rotary embedding with rotary_dim = cos.shape[-1] (python/dvattn/attention.py:82-88).
+    Used on the key side by callers; the attention ops rotate queries themselves."""
+    cos = cos.unsqueeze(unsqueeze_dim)
+    sin = sin.unsqueeze(unsqueeze_dim)
+    rotary_dim = cos.shape[-1]
+    x_rot, x_pass = x[..., :rotary_dim], x[..., rotary_dim:]
+    x_rot_emb = (x_rot * cos) + (rotate_half(x_rot) * sin)
+    return torch.cat((x_rot_emb, x_pass), dim=-1).to(x.dtype)

@@ -1,0 +1,249 @@
+"""ctypes binding of the C ABI (include/dvattn_b200.h) of libdvattn_b200.so.
+
+This is what a non-torch host (an engine written in C, Go, Java ...) sees: plain
+structs of pointers and sizes.  The helpers below fill those structs from torch
+tensors (device pointers + shapes) and call the library on the current torch stream;
+tests and the benchmark use them to exercise the boundary itself rather than the
+torch op layer.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+import torch
+
+from . import CAPI_LIB
+
+DVATTN_OK = 0
+DVATTN_ERR_INVALID_ARGUMENT = 1
+DVATTN_ERR_UNSUPPORTED = 2
+DVATTN_ERR_WORKSPACE = 3
+DVATTN_ERR_CUDA = 4
+
+DVATTN_PHASE_ALL = 0
+DVATTN_PHASE_SCHEDULE = 1
+DVATTN_PHASE_ATTEND = 2
+DVATTN_PHASE_MERGE = 3
+
+DVATTN_FLOAT32 = 0
+DVATTN_FLOAT16 = 1
+DVATTN_BFLOAT16 = 2
+
+_DTYPE = {torch.float32: DVATTN_FLOAT32, torch.float16: DVATTN_FLOAT16, torch.bfloat16: DVATTN_BFLOAT16}
+
+# Every function the header declares (checked against the header by the tests).
+EXPORTS = [
+    "dvattn_abi_version",
+    "dvattn_status_string",
+    "dvattn_paged_sdpa_workspace_size",
+    "dvattn_paged_sdpa",
+    "dvattn_paged_sdpa_phase",
+    "dvattn_varlen_paged_sdpa_workspace_size",
+    "dvattn_varlen_paged_sdpa",
+    "dvattn_rope",
+    "dvattn_varlen_rope",
+    "dvattn_lse_merge",
+]
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+
+
+class PagedArgs(ctypes.Structure):
+    _fields_ = [("dtype", _i), ("F", _i), ("W", _i), ("Hq", _i), ("Hkv", _i), ("E", _i), ("Ev", _i), ("S", _i),
+                ("R", _i), ("block_size", _i), ("max_blocks_per_seq", _i), ("num_blocks", ctypes.c_longlong),
+                ("scale", ctypes.c_float), ("out", _vp), ("queries", _vp), ("cosines", _vp), ("sines", _vp),
+                ("locations", _vp), ("fragment_lengths", _vp), ("k_cache", _vp), ("v_cache", _vp),
+                ("block_tables", _vp), ("lse_out", _vp), ("out_f32", _vp)]
+
+
+class VarlenArgs(ctypes.Structure):
+    _fields_ = [("dtype", _i), ("F", _i), ("W", _i), ("Hq", _i), ("Hkv", _i), ("E", _i), ("Ev", _i), ("T", _i),
+                ("R", _i), ("block_size", _i), ("max_blocks_per_seq", _i), ("num_blocks", ctypes.c_longlong),
+                ("scale", ctypes.c_float), ("out", _vp), ("queries", _vp), ("cosines", _vp), ("sines", _vp),
+                ("locations", _vp), ("fragment_lengths", _vp), ("k_cache", _vp), ("v_cache", _vp),
+                ("block_tables", _vp), ("cu_seqlens_q", _vp), ("cu_seqlens_k", _vp), ("lse_out", _vp),
+                ("out_f32", _vp)]
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libdvattn_b200.so and declare the signatures (no GPU needed to load)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(CAPI_LIB):
+            raise ImportError("libdvattn_b200.so is not built")
+        L = ctypes.CDLL(CAPI_LIB)
+        L.dvattn_abi_version.restype = _i
+        L.dvattn_status_string.restype = ctypes.c_char_p
+        L.dvattn_status_string.argtypes = [_i]
+        L.dvattn_paged_sdpa_workspace_size.restype = ctypes.c_size_t
+        L.dvattn_paged_sdpa_workspace_size.argtypes = [ctypes.POINTER(PagedArgs)]
+        L.dvattn_paged_sdpa.restype = _i
+        L.dvattn_paged_sdpa.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _vp]
+        L.dvattn_paged_sdpa_phase.restype = _i
+        L.dvattn_paged_sdpa_phase.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _i, _vp]
+        L.dvattn_varlen_paged_sdpa_workspace_size.restype = ctypes.c_size_t
+        L.dvattn_varlen_paged_sdpa_workspace_size.argtypes = [ctypes.POINTER(VarlenArgs)]
+        L.dvattn_varlen_paged_sdpa.restype = _i
+        L.dvattn_varlen_paged_sdpa.argtypes = [ctypes.POINTER(VarlenArgs), _vp, ctypes.c_size_t, _vp]
+        L.dvattn_rope.restype = _i
+        L.dvattn_rope.argtypes = [_i] * 7 + [_vp] * 5
+        L.dvattn_varlen_rope.restype = _i
+        L.dvattn_varlen_rope.argtypes = [_i] * 6 + [_vp] * 5
+        L.dvattn_lse_merge.restype = _i
+        L.dvattn_lse_merge.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp, _vp]
+        _lib = L
+    return _lib
+
+
+class DvattnError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {lib().dvattn_status_string(status).decode()} (status {status})")
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream: Optional[torch.cuda.Stream]) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def paged_args(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+               lse=None, out_f32=None) -> PagedArgs:
+    a = PagedArgs()
+    a.dtype = _DTYPE.get(out.dtype, -1)
+    a.F = locations.size(0)
+    a.W, a.Hq, a.S, a.Ev = out.shape
+    a.Hkv = k_cache.size(2)
+    a.E = queries.size(3)
+    a.R = cosines.size(3)
+    a.block_size = k_cache.size(1)
+    a.max_blocks_per_seq = block_tables.size(1)
+    a.num_blocks = k_cache.size(0)
+    a.scale = scale
+    a.out, a.queries, a.cosines, a.sines = out.data_ptr(), queries.data_ptr(), cosines.data_ptr(), sines.data_ptr()
+    a.locations, a.fragment_lengths = locations.data_ptr(), fragment_lengths.data_ptr()
+    a.k_cache, a.v_cache, a.block_tables = k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr()
+    a.lse_out, a.out_f32 = _ptr(lse), _ptr(out_f32)
+    return a
+
+
+def varlen_args(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+                cu_seqlens_q, lse=None, out_f32=None) -> VarlenArgs:
+    a = VarlenArgs()
+    a.dtype = _DTYPE.get(out.dtype, -1)
+    a.F = locations.size(0)
+    a.W = cu_seqlens_q.numel() - 1
+    a.T, a.Hq, a.E = queries.shape
+    a.Hkv = k_cache.size(2)
+    a.Ev = v_cache.size(3)
+    a.R = 2 * cosines.size(2)
+    a.block_size = k_cache.size(1)
+    a.max_blocks_per_seq = block_tables.size(1)
+    a.num_blocks = k_cache.size(0)
+    a.scale = scale
+    a.out, a.queries, a.cosines, a.sines = out.data_ptr(), queries.data_ptr(), cosines.data_ptr(), sines.data_ptr()
+    a.locations, a.fragment_lengths = locations.data_ptr(), fragment_lengths.data_ptr()
+    a.k_cache, a.v_cache, a.block_tables = k_cache.data_ptr(), v_cache.data_ptr(), block_tables.data_ptr()
+    a.cu_seqlens_q = cu_seqlens_q.data_ptr()
+    a.cu_seqlens_k = None
+    a.lse_out, a.out_f32 = _ptr(lse), _ptr(out_f32)
+    return a
+
+
+class PagedCall:
+    """A prepared paged-decode call through the C ABI: argument struct + workspace,
+    reusable across launches (workspace reuse is stream-ordered)."""
+
+    def __init__(self, *tensors, lse=None, out_f32=None, workspace: Optional[torch.Tensor] = None):
+        self.args = paged_args(*tensors, lse=lse, out_f32=out_f32)
+        self._keep = (tensors, lse, out_f32)
+        n = lib().dvattn_paged_sdpa_workspace_size(ctypes.byref(self.args))
+        if n == 0 and self.args.W * self.args.S > 0 and self.args.Hq > 0:
+            raise DvattnError(lib().dvattn_paged_sdpa(ctypes.byref(self.args), None, 0, None), "workspace size")
+        self.ws_bytes = n
+        if workspace is None:
+            workspace = torch.empty(max(n, 256), dtype=torch.uint8, device=tensors[0].device)
+        self.workspace = workspace
+
+    def __call__(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        st = lib().dvattn_paged_sdpa(ctypes.byref(self.args), self.workspace.data_ptr(), self.workspace.numel(),
+                                     _stream(stream))
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_paged_sdpa")
+
+    def phase(self, phase: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+        st = lib().dvattn_paged_sdpa_phase(ctypes.byref(self.args), self.workspace.data_ptr(),
+                                           self.workspace.numel(), phase, _stream(stream))
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_paged_sdpa_phase")
+
+
+class VarlenCall:
+    def __init__(self, *tensors, lse=None, out_f32=None, workspace: Optional[torch.Tensor] = None):
+        self.args = varlen_args(*tensors, lse=lse, out_f32=out_f32)
+        self._keep = (tensors, lse, out_f32)
+        n = lib().dvattn_varlen_paged_sdpa_workspace_size(ctypes.byref(self.args))
+        if n == 0 and self.args.T > 0 and self.args.Hq > 0:
+            raise DvattnError(lib().dvattn_varlen_paged_sdpa(ctypes.byref(self.args), None, 0, None), "workspace size")
+        self.ws_bytes = n
+        if workspace is None:
+            workspace = torch.empty(max(n, 256), dtype=torch.uint8, device=tensors[0].device)
+        self.workspace = workspace
+
+    def __call__(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        st = lib().dvattn_varlen_paged_sdpa(ctypes.byref(self.args), self.workspace.data_ptr(),
+                                            self.workspace.numel(), _stream(stream))
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_varlen_paged_sdpa")
+
+
+def paged_sdpa(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+               lse=None, out_f32=None):
+    PagedCall(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+              lse=lse, out_f32=out_f32)()
+    return out
+
+
+def varlen_paged_sdpa(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache,
+                      block_tables, cu_seqlens_q, lse=None, out_f32=None):
+    VarlenCall(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+               cu_seqlens_q, lse=lse, out_f32=out_f32)()
+    return out
+
+
+def rope(out, queries, cosines, sines):
+    F, W, Hq, S, E = out.shape
+    st = lib().dvattn_rope(_DTYPE.get(out.dtype, -1), F, W, Hq, S, E, cosines.size(3), out.data_ptr(),
+                           queries.data_ptr(), cosines.data_ptr(), sines.data_ptr(), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_rope")
+    return out
+
+
+def varlen_rope(out, queries, cosines, sines):
+    F, T, H, E = out.shape
+    st = lib().dvattn_varlen_rope(_DTYPE.get(out.dtype, -1), F, T, H, E, 2 * cosines.size(2), out.data_ptr(),
+                                  queries.data_ptr(), cosines.data_ptr(), sines.data_ptr(), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_varlen_rope")
+    return out
+
+
+def lse_merge(part_out, part_lse, out, lse_out=None):
+    parts = part_out.size(0)
+    Ev = part_out.size(-1)
+    rows = out.numel() // Ev
+    st = lib().dvattn_lse_merge(_DTYPE.get(out.dtype, -1), parts, rows, Ev, part_out.data_ptr(), part_lse.data_ptr(),
+                                out.data_ptr(), _ptr(lse_out), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_lse_merge")
+    return out

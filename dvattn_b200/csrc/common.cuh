@@ -1,0 +1,128 @@
+// Shared device helpers for the sm_100a DVAttn kernels: element types, cp.async with
+// zero-fill, ldmatrix / mma.sync fragments, the base-2 exponential, and the per-sequence
+// visible-length arithmetic that every kernel agrees on.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/dvattn_b200.h"
+
+namespace dvb {
+
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+
+// ----------------------------------------------------------------------------------
+// element types
+// ----------------------------------------------------------------------------------
+template <class T> struct Elem;
+template <> struct Elem<float> {
+    static constexpr int dtype = DVATTN_FLOAT32;
+    __device__ __forceinline__ static float to_f(float x) { return x; }
+    __device__ __forceinline__ static float from_f(float x) { return x; }
+};
+template <> struct Elem<__half> {
+    static constexpr int dtype = DVATTN_FLOAT16;
+    __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
+    __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
+    // two floats -> one 32-bit register of two halves (lo = a)
+    __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+        __half2 h = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static constexpr int dtype = DVATTN_BFLOAT16;
+    __device__ __forceinline__ static float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    __device__ __forceinline__ static __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+    __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+};
+
+// ----------------------------------------------------------------------------------
+// math
+// ----------------------------------------------------------------------------------
+// 2^x on the SFU (PTX ex2.approx: max relative error 2^-22 over the normal range;
+// ex2(-inf) = +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// ----------------------------------------------------------------------------------
+// cp.async (16 B, L2-only) with zero fill: copies `src_bytes` (0 or 16) bytes and fills
+// the rest of the 16-byte destination with zeros.  With src_bytes == 0 nothing is read.
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, int src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ----------------------------------------------------------------------------------
+// ldmatrix / mma.sync (m16n8k16, fp32 accumulate)
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+template <class T> struct Mma;
+template <> struct Mma<__half> {
+    __device__ __forceinline__ static void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+template <> struct Mma<__nv_bfloat16> {
+    __device__ __forceinline__ static void run(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};\n"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+};
+
+// Row of `row_bytes` (a multiple of 128) split into 16-byte chunks; chunk c of row r is
+// stored at chunk c ^ (r & 7) so that the 8 rows an ldmatrix phase reads hit 8
+// different bank groups.
+__device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
+    return static_cast<uint32_t>(row * row_bytes + ((chunk ^ (row & 7)) << 4));
+}
+
+// ----------------------------------------------------------------------------------
+// Visible keys of one turn for one query: l < L_f and l <= loc (the mask `kp > qp` of
+// python/dvattn/attention.py:48-54; negative loc means the turn is skipped,
+// src/kernels/varlen_paged_kernel_v21.cuh:76-80).  Positions past the block table
+// (max_blocks * block_size) are never visible: the reference would read past the
+// table there.
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ int visible_len(int L, int loc) {
+    int v = min(L, loc + 1);
+    return v > 0 ? v : 0;
+}
+
+}  // namespace dvb

@@ -1,0 +1,797 @@
+// Paged GQA decode for sm_100a: fused per-turn query RoPE, page-indirect K/V streaming
+// with cp.async (16-byte, zero-filled past the visible keys), QK^T and PV on tensor
+// cores with the (up to) 16 query heads of one KV head packed as the M=16 of
+// mma.sync.m16n8k16, online base-2 softmax, and a balanced split-KV schedule whose
+// pieces are merged by log-sum-exp.
+//
+// Reference path replaced: rope_gpu (src/rope.cuh:2-65) + paged_v21::
+// dvattn_paged_attention_gpu_kernel21 / dvattn_paged_attention_reduce_kernel /
+// dvattn_paged_attention_gpu (src/kernels/paged_kernel_v21.cuh:17-431).
+#include "decode.cuh"
+#include "schedule.cuh"
+
+namespace dvb {
+
+// ----------------------------------------------------------------------------------
+// query rotation of one (row ws, KV head, turn f) into shared memory.
+// rotated[e] = q[e]*c[e] - q[e+R/2]*s[e]          for e < R/2
+//            = q[e]*c[e-R/2] + q[e-R/2]*s[e-R/2]  for R/2 <= e < R
+//            = q[e]                                for e >= R
+// with c, s the first R/2 entries of the (f, ws) cos/sin row (src/rope.cuh:24-45), math
+// in f32, rounded once to T (python/dvattn/attention.py:82-88).
+// ----------------------------------------------------------------------------------
+template <class T>
+__device__ __forceinline__ float rotated_elem(const T* qrow, const float* cr, const float* sr, int e, int R) {
+    const float x = Elem<T>::to_f(qrow[e]);
+    const int h = R >> 1;
+    if (e < h) return x * cr[e] - Elem<T>::to_f(qrow[e + h]) * sr[e];
+    if (e < R) return x * cr[e - h] + Elem<T>::to_f(qrow[e - h]) * sr[e - h];
+    return x;
+}
+
+// ==================================================================================
+// tensor-core kernel (f16 / bf16)
+// ==================================================================================
+template <class T, int E, int WARPS, int STAGES>
+struct TcCfg {
+    static constexpr int NT = WARPS * 32;
+    static constexpr int TILE = WARPS * 16;        // keys per pipeline stage
+    static constexpr int ROWB = E * 2;             // bytes of one K/V/Q row
+    static constexpr int CPR = ROWB / 16;          // 16-byte chunks per row
+    static constexpr int STAGE_BYTES = TILE * ROWB;
+    static constexpr int KS = E / 16;              // k16 steps of QK^T
+    static constexpr bool QREG = (E <= 128);       // keep Q fragments in registers
+    static constexpr size_t SMEM = 2ull * STAGES * STAGE_BYTES + 16 * ROWB + 16 * E * 4 + WARPS * 16 * 2 * 4 + 16 * 4;
+};
+
+template <class T, int E, int WARPS, int STAGES>
+__global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
+    using C = TcCfg<T, E, WARPS, STAGES>;
+    constexpr int NT = C::NT, TILE = C::TILE, ROWB = C::ROWB, CPR = C::CPR;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t* sK = smem;
+    uint8_t* sV = sK + STAGES * C::STAGE_BYTES;
+    uint8_t* sQ = sV + STAGES * C::STAGE_BYTES;
+    float* sO = reinterpret_cast<float*>(sQ + 16 * ROWB);
+    float* sML = sO + 16 * E;           // [WARPS][16][2]
+    float* sLse = sML + WARPS * 16 * 2; // [16]
+
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const DecodeSched sch = *p.sched;
+    const int c = blockIdx.x;
+    if (c >= sch.n_eff) return;
+    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    if (u0 >= u1) return;
+    const int ws0 = find_row<NT>(p, u0);
+
+    const T* __restrict__ kc = static_cast<const T*>(p.k);
+    const T* __restrict__ vc = static_cast<const T*>(p.v);
+    const uint32_t sK0 = smem_u32(sK), sV0 = smem_u32(sV), sQ0 = smem_u32(sQ);
+
+    // ---- producer: issue one tile of K and V rows into stage `st` ----
+    auto issue = [&](const TileDesc& d, int st) {
+        const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+        const uint32_t kd = sK0 + st * C::STAGE_BYTES, vd = sV0 + st * C::STAGE_BYTES;
+#pragma unroll
+        for (int i = 0; i < TILE * CPR / NT; ++i) {
+            const int idx = i * NT + tid;
+            const int r = idx / CPR, ch = idx % CPR;
+            const T* ks = kc;
+            const T* vs = vc;
+            int bytes = 0;
+            if (r < d.n) {
+                const int pos = d.pos0 + r;
+                const int page = __ldg(btw + pos / p.BS);
+                if (p.NB <= 0 || (page >= 0 && page < p.NB)) {
+                    const size_t row = ((size_t)page * p.BS + pos % p.BS) * p.Hkv + d.hkv;
+                    ks = kc + row * E + ch * 8;
+                    vs = vc + row * E + ch * 8;
+                    bytes = 16;
+                }
+            }
+            cp_async16_zfill(kd + swz(r, ch, ROWB), ks, bytes);
+            cp_async16_zfill(vd + swz(r, ch, ROWB), vs, bytes);
+        }
+    };
+
+    for (int i = tid; i < 16 * E; i += NT) sO[i] = 0.f;
+
+    TileIter<TILE> prod, cons;
+    prod.init(p, ws0, u0, u1);
+    cons = prod;
+#pragma unroll
+    for (int st = 0; st < STAGES - 1; ++st) {
+        TileDesc d;
+        if (prod.next(p, d)) issue(d, st);
+        cp_async_commit();
+    }
+
+    // ---- consumer state (per warp: 16 rows = query heads) ----
+    uint32_t qf[C::QREG ? C::KS : 1][4];
+    float o[E / 8][4];
+    float m0 = 0.f, m1 = 0.f, l0 = 0.f, l1 = 0.f;
+    int st_c = 0, st_p = STAGES - 1;
+    TileDesc d;
+    while (cons.next(p, d)) {
+        if (d.new_seg) {
+            m0 = m1 = neg_inf();
+            l0 = l1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        }
+        if (d.new_turn) {
+            __syncthreads();
+            const int w = d.ws / p.S;
+            const float* cr = p.cos + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
+            const float* sr = p.sin + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
+            const int s = d.ws - w * p.S;
+            for (int idx = tid; idx < 16 * CPR; idx += NT) {
+                const int g = idx / CPR, ch = idx % CPR;
+                uint32_t pk[4] = {0u, 0u, 0u, 0u};
+                if (g < p.gqa) {
+                    const int hq = d.hkv * p.gqa + g;
+                    const T* qrow = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int e = ch * 8 + 2 * j;
+                        pk[j] = Elem<T>::pack2(rotated_elem(qrow, cr, sr, e, p.R), rotated_elem(qrow, cr, sr, e + 1, p.R));
+                    }
+                }
+                *reinterpret_cast<uint4*>(sQ + swz(g, ch, ROWB)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+            __syncthreads();
+            if constexpr (C::QREG) {
+#pragma unroll
+                for (int kk = 0; kk < C::KS; ++kk)
+                    ldsm_x4(sQ0 + swz((lane & 7) + ((lane >> 3) & 1) * 8, kk * 2 + (lane >> 4), ROWB), qf[kk][0],
+                            qf[kk][1], qf[kk][2], qf[kk][3]);
+            }
+        }
+
+        {
+            TileDesc dp;
+            if (prod.next(p, dp)) issue(dp, st_p);
+            cp_async_commit();
+        }
+        cp_async_wait<STAGES - 1>();
+        __syncthreads();
+
+        const int rb = wid * 16;
+        const int nv = d.n - rb;
+        if (nv > 0) {
+            const uint32_t kb = sK0 + st_c * C::STAGE_BYTES, vb = sV0 + st_c * C::STAGE_BYTES;
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < C::KS; ++kk) {
+                uint32_t a[4];
+                if constexpr (C::QREG) {
+                    a[0] = qf[kk][0]; a[1] = qf[kk][1]; a[2] = qf[kk][2]; a[3] = qf[kk][3];
+                } else {
+                    ldsm_x4(sQ0 + swz((lane & 7) + ((lane >> 3) & 1) * 8, kk * 2 + (lane >> 4), ROWB), a[0], a[1], a[2], a[3]);
+                }
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kb + swz(rb + (lane & 7) + ((lane >> 4) << 3), kk * 2 + ((lane >> 3) & 1), ROWB), b0, b1, b2, b3);
+                Mma<T>::run(sc[0], a, b0, b1);
+                Mma<T>::run(sc[1], a, b2, b3);
+            }
+            // mask + online softmax (rows r = lane/4 and r + 8)
+            float mx0 = neg_inf(), mx1 = neg_inf();
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col = nt * 8 + 2 * (lane & 3) + (j & 1);
+                    const float x = col < nv ? sc[nt][j] * p.scale_log2 : neg_inf();
+                    sc[nt][j] = x;
+                    if (j < 2) mx0 = fmaxf(mx0, x); else mx1 = fmaxf(mx1, x);
+                }
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+            const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+            m0 = n0;
+            m1 = n1;
+            float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sc[nt][0] = fast_exp2(sc[nt][0] - n0);
+                sc[nt][1] = fast_exp2(sc[nt][1] - n0);
+                sc[nt][2] = fast_exp2(sc[nt][2] - n1);
+                sc[nt][3] = fast_exp2(sc[nt][3] - n1);
+                ps0 += sc[nt][0] + sc[nt][1];
+                ps1 += sc[nt][2] + sc[nt][3];
+            }
+            l0 = l0 * al0 + ps0;
+            l1 = l1 * al1 + ps1;
+#pragma unroll
+            for (int j = 0; j < E / 8; ++j) {
+                o[j][0] *= al0; o[j][1] *= al0;
+                o[j][2] *= al1; o[j][3] *= al1;
+            }
+            uint32_t pa[4];
+            pa[0] = Elem<T>::pack2(sc[0][0], sc[0][1]);
+            pa[1] = Elem<T>::pack2(sc[0][2], sc[0][3]);
+            pa[2] = Elem<T>::pack2(sc[1][0], sc[1][1]);
+            pa[3] = Elem<T>::pack2(sc[1][2], sc[1][3]);
+#pragma unroll
+            for (int np = 0; np < E / 16; ++np) {
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vb + swz(rb + (lane & 7) + (((lane >> 3) & 1) << 3), 2 * np + (lane >> 4), ROWB), b0, b1, b2, b3);
+                Mma<T>::run(o[2 * np], pa, b0, b1);
+                Mma<T>::run(o[2 * np + 1], pa, b2, b3);
+            }
+        }
+
+        if (d.seg_last) {
+            // ---- combine the WARPS per-warp states of this segment piece ----
+            float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+            lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
+            float lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+            lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
+            const int r0 = lane >> 2;
+            if ((lane & 3) == 0) {
+                sML[(wid * 16 + r0) * 2 + 0] = m0;
+                sML[(wid * 16 + r0) * 2 + 1] = lt0;
+                sML[(wid * 16 + r0 + 8) * 2 + 0] = m1;
+                sML[(wid * 16 + r0 + 8) * 2 + 1] = lt1;
+            }
+            __syncthreads();
+            float M0 = neg_inf(), M1 = neg_inf();
+#pragma unroll
+            for (int w2 = 0; w2 < WARPS; ++w2) {
+                M0 = fmaxf(M0, sML[(w2 * 16 + r0) * 2]);
+                M1 = fmaxf(M1, sML[(w2 * 16 + r0 + 8) * 2]);
+            }
+            float S0 = 0.f, S1 = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < WARPS; ++w2) {
+                const float a0 = sML[(w2 * 16 + r0) * 2], a1 = sML[(w2 * 16 + r0 + 8) * 2];
+                if (a0 != neg_inf()) S0 += sML[(w2 * 16 + r0) * 2 + 1] * fast_exp2(a0 - M0);
+                if (a1 != neg_inf()) S1 += sML[(w2 * 16 + r0 + 8) * 2 + 1] * fast_exp2(a1 - M1);
+            }
+            const float f0 = (m0 != neg_inf() && S0 > 0.f) ? fast_exp2(m0 - M0) / S0 : 0.f;
+            const float f1 = (m1 != neg_inf() && S1 > 0.f) ? fast_exp2(m1 - M1) / S1 : 0.f;
+            if (wid == 0 && (lane & 3) == 0) {
+                sLse[r0] = S0 > 0.f ? M0 + __log2f(S0) : neg_inf();
+                sLse[r0 + 8] = S1 > 0.f ? M1 + __log2f(S1) : neg_inf();
+            }
+            // fixed-order sum over warps (deterministic)
+#pragma unroll 1
+            for (int w2 = 0; w2 < WARPS; ++w2) {
+                if (wid == w2) {
+#pragma unroll
+                    for (int j = 0; j < E / 8; ++j) {
+                        const int e = j * 8 + 2 * (lane & 3);
+                        float2* a = reinterpret_cast<float2*>(sO + r0 * E + e);
+                        float2* b = reinterpret_cast<float2*>(sO + (r0 + 8) * E + e);
+                        float2 va = *a, vb2 = *b;
+                        va.x += o[j][0] * f0; va.y += o[j][1] * f0;
+                        vb2.x += o[j][2] * f1; vb2.y += o[j][3] * f1;
+                        *a = va;
+                        *b = vb2;
+                    }
+                }
+                __syncthreads();
+            }
+            // ---- write: final output if this CTA saw the whole segment, else a partial ----
+            const int w = d.ws / p.S, s = d.ws - w * p.S;
+            if (d.seg_complete) {
+                for (int idx = tid * 4; idx < 16 * E; idx += NT * 4) {
+                    const int g = idx / E, e = idx % E;
+                    float4 v = *reinterpret_cast<float4*>(sO + idx);
+                    *reinterpret_cast<float4*>(sO + idx) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (g < p.gqa) {
+                        const size_t orow = ((size_t)w * p.Hq + d.hkv * p.gqa + g) * p.S + s;
+                        T* op = static_cast<T*>(p.out) + orow * E + e;
+                        uint2 pk;
+                        pk.x = Elem<T>::pack2(v.x, v.y);
+                        pk.y = Elem<T>::pack2(v.z, v.w);
+                        *reinterpret_cast<uint2*>(op) = pk;
+                        if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) = v;
+                        if (p.lse_out && e == 0) p.lse_out[orow] = sLse[g] * kLn2;
+                    }
+                }
+            } else {
+                const int slot = 2 * c + (d.first_piece ? 0 : 1);
+                for (int idx = tid * 4; idx < 16 * E; idx += NT * 4) {
+                    float4 v = *reinterpret_cast<float4*>(sO + idx);
+                    *reinterpret_cast<float4*>(sO + idx) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float4*>(p.part_o + (size_t)slot * 16 * E + idx) = v;
+                }
+                if (tid < 16) p.part_lse[slot * 16 + tid] = sLse[tid];
+            }
+        }
+        __syncthreads();
+        st_c = (st_c + 1 == STAGES) ? 0 : st_c + 1;
+        st_p = (st_p + 1 == STAGES) ? 0 : st_p + 1;
+    }
+    cp_async_wait<0>();
+}
+
+// ==================================================================================
+// f32 kernel (CUDA cores; tensor-core tf32 would miss the 1e-5 f32 tolerance)
+// thread t owns query head h = t / 8 for scores and the output columns
+// e = 4 * ((t % 8) + 8k) .. +3, so no cross-thread merge is needed.
+// ==================================================================================
+template <int E, int STAGES>
+struct F32Cfg {
+    static constexpr int NT = 128;
+    static constexpr int TILE = 32;
+    static constexpr int LD = E + 4;          // padded row (floats)
+    static constexpr int STAGE_F = TILE * LD; // floats per stage
+    static constexpr int CPR = E / 4;         // 16-byte chunks per row
+    static constexpr size_t SMEM = (2ull * STAGES * STAGE_F + 16 * LD + 16 * TILE) * 4;
+};
+
+template <int E, int STAGES>
+__global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
+    using C = F32Cfg<E, STAGES>;
+    constexpr int NT = C::NT, TILE = C::TILE, LD = C::LD, CPR = C::CPR;
+    constexpr int EC = E / 32;  // float4 column chunks per thread
+    extern __shared__ __align__(1024) uint8_t smem[];
+    float* sK = reinterpret_cast<float*>(smem);
+    float* sV = sK + STAGES * C::STAGE_F;
+    float* sQ = sV + STAGES * C::STAGE_F;
+    float* sP = sQ + 16 * LD;
+
+    const int tid = threadIdx.x;
+    const DecodeSched sch = *p.sched;
+    const int c = blockIdx.x;
+    if (c >= sch.n_eff) return;
+    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    if (u0 >= u1) return;
+    const int ws0 = find_row<NT>(p, u0);
+    const float* __restrict__ kc = static_cast<const float*>(p.k);
+    const float* __restrict__ vc = static_cast<const float*>(p.v);
+
+    auto issue = [&](const TileDesc& d, int st) {
+        const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+        float* kd = sK + st * C::STAGE_F;
+        float* vd = sV + st * C::STAGE_F;
+#pragma unroll
+        for (int i = 0; i < TILE * CPR / NT; ++i) {
+            const int idx = i * NT + tid;
+            const int r = idx / CPR, ch = idx % CPR;
+            const float* ks = kc;
+            const float* vs = vc;
+            int bytes = 0;
+            if (r < d.n) {
+                const int pos = d.pos0 + r;
+                const int page = __ldg(btw + pos / p.BS);
+                if (p.NB <= 0 || (page >= 0 && page < p.NB)) {
+                    const size_t row = ((size_t)page * p.BS + pos % p.BS) * p.Hkv + d.hkv;
+                    ks = kc + row * E + ch * 4;
+                    vs = vc + row * E + ch * 4;
+                    bytes = 16;
+                }
+            }
+            cp_async16_zfill(smem_u32(kd + r * LD + ch * 4), ks, bytes);
+            cp_async16_zfill(smem_u32(vd + r * LD + ch * 4), vs, bytes);
+        }
+    };
+
+    TileIter<TILE> prod, cons;
+    prod.init(p, ws0, u0, u1);
+    cons = prod;
+#pragma unroll
+    for (int st = 0; st < STAGES - 1; ++st) {
+        TileDesc d;
+        if (prod.next(p, d)) issue(d, st);
+        cp_async_commit();
+    }
+
+    const int h = tid >> 3, sub = tid & 7;
+    float o[EC][4];
+    float m = 0.f, l = 0.f;
+    int st_c = 0, st_p = STAGES - 1;
+    TileDesc d;
+    while (cons.next(p, d)) {
+        if (d.new_seg) {
+            m = neg_inf();
+            l = 0.f;
+#pragma unroll
+            for (int j = 0; j < EC; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        }
+        if (d.new_turn) {
+            __syncthreads();
+            const int w = d.ws / p.S, s = d.ws - w * p.S;
+            const float* cr = p.cos + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
+            const float* sr = p.sin + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
+            for (int idx = tid; idx < 16 * E; idx += NT) {
+                const int g = idx / E, e = idx % E;
+                float x = 0.f;
+                if (g < p.gqa) {
+                    const float* qrow = static_cast<const float*>(p.q) + (((size_t)w * p.Hq + d.hkv * p.gqa + g) * p.S + s) * E;
+                    x = rotated_elem(qrow, cr, sr, e, p.R);
+                }
+                sQ[g * LD + e] = x;
+            }
+        }
+        {
+            TileDesc dp;
+            if (prod.next(p, dp)) issue(dp, st_p);
+            cp_async_commit();
+        }
+        cp_async_wait<STAGES - 1>();
+        __syncthreads();
+
+        const float* kb = sK + st_c * C::STAGE_F;
+        const float* vb = sV + st_c * C::STAGE_F;
+        // scores of head h for keys sub, sub+8, sub+16, sub+24
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int e = 0; e < E; e += 4) {
+            const float4 qv = *reinterpret_cast<const float4*>(sQ + h * LD + e);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 kv = *reinterpret_cast<const float4*>(kb + (sub + 8 * i) * LD + e);
+                sc[i] = fmaf(qv.x, kv.x, sc[i]);
+                sc[i] = fmaf(qv.y, kv.y, sc[i]);
+                sc[i] = fmaf(qv.z, kv.z, sc[i]);
+                sc[i] = fmaf(qv.w, kv.w, sc[i]);
+            }
+        }
+        float mx = neg_inf();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            sc[i] = (sub + 8 * i) < d.n ? sc[i] * p.scale_log2 : neg_inf();
+            mx = fmaxf(mx, sc[i]);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float mn = fmaxf(m, mx);
+        const float al = fast_exp2(m - mn);
+        m = mn;
+        float ps = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float pv = fast_exp2(sc[i] - mn);
+            ps += pv;
+            sP[h * TILE + sub + 8 * i] = pv;
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        l = l * al + ps;
+#pragma unroll
+        for (int j = 0; j < EC; ++j) {
+            o[j][0] *= al; o[j][1] *= al; o[j][2] *= al; o[j][3] *= al;
+        }
+        __syncwarp();
+        // head h's probabilities were written by the 8 lanes of this same warp group
+        for (int r = 0; r < d.n; ++r) {
+            const float pv = sP[h * TILE + r];
+#pragma unroll
+            for (int j = 0; j < EC; ++j) {
+                const float4 vv = *reinterpret_cast<const float4*>(vb + r * LD + 4 * (sub + 8 * j));
+                o[j][0] = fmaf(pv, vv.x, o[j][0]);
+                o[j][1] = fmaf(pv, vv.y, o[j][1]);
+                o[j][2] = fmaf(pv, vv.z, o[j][2]);
+                o[j][3] = fmaf(pv, vv.w, o[j][3]);
+            }
+        }
+
+        if (d.seg_last) {
+            const int w = d.ws / p.S, s = d.ws - w * p.S;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            const float lse2 = l > 0.f ? m + __log2f(l) : neg_inf();
+            if (d.seg_complete) {
+                if (h < p.gqa) {
+                    const size_t orow = ((size_t)w * p.Hq + d.hkv * p.gqa + h) * p.S + s;
+                    float* op = static_cast<float*>(p.out) + orow * E;
+#pragma unroll
+                    for (int j = 0; j < EC; ++j) {
+                        const float4 v = make_float4(o[j][0] * inv, o[j][1] * inv, o[j][2] * inv, o[j][3] * inv);
+                        *reinterpret_cast<float4*>(op + 4 * (sub + 8 * j)) = v;
+                        if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + 4 * (sub + 8 * j)) = v;
+                    }
+                    if (p.lse_out && sub == 0) p.lse_out[orow] = lse2 * kLn2;
+                }
+            } else {
+                const int slot = 2 * c + (d.first_piece ? 0 : 1);
+                float* po = p.part_o + ((size_t)slot * 16 + h) * E;
+#pragma unroll
+                for (int j = 0; j < EC; ++j)
+                    *reinterpret_cast<float4*>(po + 4 * (sub + 8 * j)) =
+                        make_float4(o[j][0] * inv, o[j][1] * inv, o[j][2] * inv, o[j][3] * inv);
+                if (sub == 0) p.part_lse[slot * 16 + h] = lse2;
+            }
+        }
+        __syncthreads();
+        st_c = (st_c + 1 == STAGES) ? 0 : st_c + 1;
+        st_p = (st_p + 1 == STAGES) ? 0 : st_p + 1;
+    }
+    cp_async_wait<0>();
+}
+
+// ==================================================================================
+// merge of split segments (and zeros for rows that see no key)
+// one CTA per segment, 128 threads: thread t -> row t/8, columns 4*((t%8) + 8k)
+// ==================================================================================
+template <class T>
+__global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E) {
+    const int g_seg = blockIdx.x;
+    const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
+    const int tid = threadIdx.x, r = tid >> 3, sub = tid & 7;
+    const DecodeSched sch = *p.sched;
+    const long long P0 = p.P[ws], V = p.P[ws + 1] - P0;
+    const int w = ws / p.S, s = ws - w * p.S;
+    const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
+    if (V == 0) {
+        if (r < p.gqa) {
+            T* op = static_cast<T*>(p.out) + orow * E;
+            for (int e = 4 * sub; e < E; e += 32) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) op[e + j] = Elem<T>::from_f(0.f);
+                if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            if (p.lse_out && sub == 0) p.lse_out[orow] = neg_inf();
+        }
+        return;
+    }
+    const long long b = P0 * p.Hkv + hkv * V;
+    const int n = sch.n_eff;
+    const int ca = cta_of(b, sch.U, n), cb = cta_of(b + V - 1, sch.U, n);
+    if (ca == cb || r >= p.gqa) return;
+
+    float lmax = neg_inf();
+    for (int c = ca; c <= cb; ++c) {
+        const int slot = (c == ca && cta_start(ca, sch.U, n) < b) ? 2 * ca + 1 : 2 * c;
+        lmax = fmaxf(lmax, p.part_lse[slot * 16 + r]);
+    }
+    float acc[32];
+    const int nchunk = E / 32;  // float4 chunks per thread
+    for (int j = 0; j < 4 * nchunk; ++j) acc[j] = 0.f;
+    float den = 0.f;
+    for (int c = ca; c <= cb; ++c) {
+        const int slot = (c == ca && cta_start(ca, sch.U, n) < b) ? 2 * ca + 1 : 2 * c;
+        const float ls = p.part_lse[slot * 16 + r];
+        if (ls == neg_inf()) continue;
+        const float wgt = fast_exp2(ls - lmax);
+        den += wgt;
+        const float* po = p.part_o + ((size_t)slot * 16 + r) * E;
+        for (int j = 0; j < nchunk; ++j) {
+            const float4 v = *reinterpret_cast<const float4*>(po + 4 * (sub + 8 * j));
+            acc[4 * j + 0] += wgt * v.x;
+            acc[4 * j + 1] += wgt * v.y;
+            acc[4 * j + 2] += wgt * v.z;
+            acc[4 * j + 3] += wgt * v.w;
+        }
+    }
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    T* op = static_cast<T*>(p.out) + orow * E;
+    for (int j = 0; j < nchunk; ++j) {
+        const int e = 4 * (sub + 8 * j);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) op[e + q] = Elem<T>::from_f(acc[4 * j + q] * inv);
+        if (p.out_f32)
+            *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) =
+                make_float4(acc[4 * j] * inv, acc[4 * j + 1] * inv, acc[4 * j + 2] * inv, acc[4 * j + 3] * inv);
+    }
+    if (p.lse_out && sub == 0) p.lse_out[orow] = den > 0.f ? (lmax + __log2f(den)) * kLn2 : neg_inf();
+}
+
+// ==================================================================================
+// host side
+// ==================================================================================
+namespace {
+
+struct KernelChoice {
+    const void* fn;
+    size_t smem;
+    int nt;
+    int min_units;
+};
+
+template <class T, int E>
+KernelChoice tc_choice() {
+    constexpr int WARPS = 4, STAGES = (E <= 128) ? 3 : 2;
+    using C = TcCfg<T, E, WARPS, STAGES>;
+    return {reinterpret_cast<const void*>(&decode_tc_kernel<T, E, WARPS, STAGES>), C::SMEM, C::NT, C::TILE};
+}
+template <int E>
+KernelChoice f32_choice() {
+    constexpr int STAGES = (E <= 128) ? 3 : 2;
+    using C = F32Cfg<E, STAGES>;
+    return {reinterpret_cast<const void*>(&decode_f32_kernel<E, STAGES>), C::SMEM, C::NT, C::TILE};
+}
+
+bool pick_kernel(int dtype, int E, KernelChoice& kc) {
+    switch (dtype) {
+        case DVATTN_FLOAT16:
+            if (E == 64) { kc = tc_choice<__half, 64>(); return true; }
+            if (E == 128) { kc = tc_choice<__half, 128>(); return true; }
+            if (E == 256) { kc = tc_choice<__half, 256>(); return true; }
+            return false;
+        case DVATTN_BFLOAT16:
+            if (E == 64) { kc = tc_choice<__nv_bfloat16, 64>(); return true; }
+            if (E == 128) { kc = tc_choice<__nv_bfloat16, 128>(); return true; }
+            if (E == 256) { kc = tc_choice<__nv_bfloat16, 256>(); return true; }
+            return false;
+        case DVATTN_FLOAT32:
+            if (E == 64) { kc = f32_choice<64>(); return true; }
+            if (E == 128) { kc = f32_choice<128>(); return true; }
+            if (E == 256) { kc = f32_choice<256>(); return true; }
+            return false;
+        default:
+            return false;
+    }
+}
+
+}  // namespace
+
+int decode_validate(const dvattn_paged_args* a) {
+    if (!a) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->dtype < 0 || a->dtype > 2) return DVATTN_ERR_UNSUPPORTED;
+    if (a->F < 0 || a->W < 0 || a->Hq < 0 || a->Hkv <= 0 || a->E <= 0 || a->Ev <= 0 || a->S < 0 || a->R < 0 ||
+        a->block_size <= 0 || a->max_blocks_per_seq < 0)
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->R > a->E || (a->R & 1)) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->Hq % a->Hkv) return DVATTN_ERR_INVALID_ARGUMENT;
+    const int gqa = a->Hq / a->Hkv;
+    if (gqa > 16 || (a->Hq > 0 && gqa < 1)) return DVATTN_ERR_UNSUPPORTED;
+    if (a->E != a->Ev) return DVATTN_ERR_UNSUPPORTED;
+    KernelChoice kc;
+    if (!pick_kernel(a->dtype, a->E, kc)) return DVATTN_ERR_UNSUPPORTED;
+    return DVATTN_OK;
+}
+
+static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return DVATTN_ERR_CUDA;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return DVATTN_ERR_CUDA;
+    if (cudaFuncSetAttribute(kc.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kc.smem) != cudaSuccess)
+        return DVATTN_ERR_CUDA;
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kc.fn, kc.nt, kc.smem) != cudaSuccess) return DVATTN_ERR_CUDA;
+    if (occ < 1) occ = 1;
+    n_launch = sms * occ;
+    return DVATTN_OK;
+}
+
+struct DecodeLayout {
+    size_t off_P, off_rs, off_po, off_pl, total;
+};
+static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen) {
+    auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
+    DecodeLayout L;
+    L.off_P = 256;
+    L.off_rs = L.off_P + up(sizeof(long long) * (size_t)(WS + 1));
+    L.off_po = L.off_rs + (varlen ? up(sizeof(int) * (size_t)WS) : 0);
+    L.off_pl = L.off_po + up(sizeof(float) * (size_t)n_launch * 2 * 16 * E);
+    L.total = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * 16);
+    return L;
+}
+
+size_t decode_workspace_size(const dvattn_paged_args* a) {
+    if (decode_validate(a) != DVATTN_OK) return 0;
+    KernelChoice kc;
+    pick_kernel(a->dtype, a->E, kc);
+    int n_launch = 0;
+    if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
+    return decode_layout(a->W * a->S, a->E, n_launch, false).total;
+}
+
+// Runs prep -> split kernel -> merge for a filled PagedParams (pointers, sizes, R,
+// cs_stride, cu_q/nseq); fills the workspace-derived fields.
+static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
+    KernelChoice kc;
+    if (!pick_kernel(dtype, p.E, kc)) return DVATTN_ERR_UNSUPPORTED;
+    int n_launch = 0;
+    int st = device_sms_and_occ(kc, n_launch);
+    if (st != DVATTN_OK) return st;
+    const DecodeLayout L = decode_layout(p.WS, p.E, n_launch, p.cu_q != nullptr);
+    if (!workspace || wbytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255)) return DVATTN_ERR_WORKSPACE;
+    char* wsb = static_cast<char*>(workspace);
+    p.sched = reinterpret_cast<DecodeSched*>(wsb);
+    p.P = reinterpret_cast<long long*>(wsb + L.off_P);
+    p.row_seq = p.cu_q ? reinterpret_cast<int*>(wsb + L.off_rs) : nullptr;
+    p.part_o = reinterpret_cast<float*>(wsb + L.off_po);
+    p.part_lse = reinterpret_cast<float*>(wsb + L.off_pl);
+    p.n_launch = n_launch;
+    p.min_units = kc.min_units;
+
+    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) decode_prep_kernel<<<1, 1024, 0, stream>>>(p);
+    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_ATTEND) {
+        void* args[] = {&p};
+        if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)
+            return DVATTN_ERR_CUDA;
+    }
+    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_MERGE) {
+        const unsigned segs = (unsigned)p.WS * (unsigned)p.Hkv;
+        switch (dtype) {
+            case DVATTN_FLOAT16: decode_merge_kernel<__half><<<segs, 128, 0, stream>>>(p, p.E); break;
+            case DVATTN_BFLOAT16: decode_merge_kernel<__nv_bfloat16><<<segs, 128, 0, stream>>>(p, p.E); break;
+            default: decode_merge_kernel<float><<<segs, 128, 0, stream>>>(p, p.E); break;
+        }
+    }
+    return cudaGetLastError() == cudaSuccess ? DVATTN_OK : DVATTN_ERR_CUDA;
+}
+
+static bool misaligned16(const void* a) { return (reinterpret_cast<uintptr_t>(a) & 15) != 0; }
+
+int decode_launch(const dvattn_paged_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
+    if (phase < DVATTN_PHASE_ALL || phase > DVATTN_PHASE_MERGE) return DVATTN_ERR_INVALID_ARGUMENT;
+    int st = decode_validate(a);
+    if (st != DVATTN_OK) return st;
+    const int WS = a->W * a->S;
+    if (WS == 0 || a->Hq == 0) return DVATTN_OK;
+    if (!a->out || !a->queries || !a->k_cache || !a->v_cache || !a->block_tables ||
+        (a->F > 0 && (!a->locations || !a->fragment_lengths)))
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->R > 0 && (!a->cosines || !a->sines)) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (misaligned16(a->queries) || misaligned16(a->k_cache) || misaligned16(a->v_cache) || misaligned16(a->out) ||
+        (a->out_f32 && misaligned16(a->out_f32)))
+        return DVATTN_ERR_INVALID_ARGUMENT;
+
+    PagedParams p{};
+    p.F = a->F; p.W = a->W; p.Hq = a->Hq; p.Hkv = a->Hkv; p.E = a->E; p.S = a->S; p.R = a->R;
+    p.BS = a->block_size; p.maxb = a->max_blocks_per_seq; p.WS = WS; p.gqa = a->Hq / a->Hkv;
+    const long long cap = (long long)a->max_blocks_per_seq * a->block_size;
+    p.cap = cap > 0x7fffffffLL ? 0x7fffffff : (int)cap;
+    p.NB = a->num_blocks;
+    p.scale_log2 = a->scale * kLog2e;
+    p.out = a->out; p.q = a->queries; p.cos = a->cosines; p.sin = a->sines; p.loc = a->locations;
+    p.L = a->fragment_lengths; p.k = a->k_cache; p.v = a->v_cache; p.bt = a->block_tables;
+    p.lse_out = a->lse_out; p.out_f32 = a->out_f32;
+    p.cu_q = nullptr; p.nseq = 0; p.cs_stride = a->R;
+    return run_schedule(p, a->dtype, workspace, wbytes, stream, phase);
+}
+
+// ---------------------------------------------------------------------------------
+// varlen prefill through the same schedule: packed token t is query row ws = t of a
+// decode with W = T, S = 1; its block-table row comes from cu_seqlens_q and its cos/sin
+// rows are half width ([F,T,R/2]).
+// ---------------------------------------------------------------------------------
+static dvattn_paged_args varlen_as_paged(const dvattn_varlen_args* v) {
+    dvattn_paged_args a{};
+    a.dtype = v->dtype; a.F = v->F; a.W = v->T; a.Hq = v->Hq; a.Hkv = v->Hkv; a.E = v->E; a.Ev = v->Ev; a.S = 1;
+    a.R = v->R; a.block_size = v->block_size; a.max_blocks_per_seq = v->max_blocks_per_seq;
+    a.num_blocks = v->num_blocks; a.scale = v->scale;
+    return a;
+}
+
+size_t varlen_workspace_size(const dvattn_varlen_args* v) {
+    if (!v || v->W < 0 || v->T < 0) return 0;
+    dvattn_paged_args a = varlen_as_paged(v);
+    if (decode_validate(&a) != DVATTN_OK) return 0;
+    KernelChoice kc;
+    pick_kernel(a.dtype, a.E, kc);
+    int n_launch = 0;
+    if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
+    return decode_layout(v->T, v->E, n_launch, true).total;
+}
+
+int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, cudaStream_t stream) {
+    if (!v || v->W < 0 || v->T < 0) return DVATTN_ERR_INVALID_ARGUMENT;
+    dvattn_paged_args a = varlen_as_paged(v);
+    int st = decode_validate(&a);
+    if (st != DVATTN_OK) return st;
+    if (v->T == 0 || v->Hq == 0) return DVATTN_OK;
+    if (!v->out || !v->queries || !v->k_cache || !v->v_cache || !v->block_tables || !v->cu_seqlens_q ||
+        (v->F > 0 && (!v->locations || !v->fragment_lengths)))
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    if (v->R > 0 && (!v->cosines || !v->sines)) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (misaligned16(v->queries) || misaligned16(v->k_cache) || misaligned16(v->v_cache) || misaligned16(v->out) ||
+        (v->out_f32 && misaligned16(v->out_f32)))
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    PagedParams p{};
+    p.F = v->F; p.W = v->T; p.Hq = v->Hq; p.Hkv = v->Hkv; p.E = v->E; p.S = 1; p.R = v->R;
+    p.BS = v->block_size; p.maxb = v->max_blocks_per_seq; p.WS = v->T; p.gqa = v->Hq / v->Hkv;
+    const long long cap = (long long)v->max_blocks_per_seq * v->block_size;
+    p.cap = cap > 0x7fffffffLL ? 0x7fffffff : (int)cap;
+    p.NB = v->num_blocks;
+    p.scale_log2 = v->scale * kLog2e;
+    p.out = v->out; p.q = v->queries; p.cos = v->cosines; p.sin = v->sines; p.loc = v->locations;
+    p.L = v->fragment_lengths; p.k = v->k_cache; p.v = v->v_cache; p.bt = v->block_tables;
+    p.lse_out = v->lse_out; p.out_f32 = v->out_f32;
+    p.cu_q = v->cu_seqlens_q; p.nseq = v->W; p.cs_stride = v->R / 2;
+    return run_schedule(p, v->dtype, workspace, wbytes, stream, DVATTN_PHASE_ALL);
+}
+
+}  // namespace dvb

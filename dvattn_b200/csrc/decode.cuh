@@ -1,0 +1,23 @@
+// Host entry points of the paged-decode machinery (decode.cu) and the standalone
+// rotation / merge kernels (rope.cu, merge.cu).  All return DVATTN_* status codes.
+#pragma once
+
+#include "common.cuh"
+
+namespace dvb {
+
+int decode_validate(const dvattn_paged_args* a);
+size_t decode_workspace_size(const dvattn_paged_args* a);
+int decode_launch(const dvattn_paged_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
+
+size_t varlen_workspace_size(const dvattn_varlen_args* a);
+int varlen_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream);
+
+int rope_launch(int dtype, int F, int W, int Hq, int S, int E, int R, void* out, const void* q, const float* cos,
+                const float* sin, cudaStream_t stream);
+int varlen_rope_launch(int dtype, int F, int T, int H, int E, int R, void* out, const void* q, const float* cos,
+                       const float* sin, cudaStream_t stream);
+int lse_merge_launch(int dtype, int num_parts, long long rows, int Ev, const float* part_out, const float* part_lse,
+                     void* out, float* lse_out, cudaStream_t stream);
+
+}  // namespace dvb

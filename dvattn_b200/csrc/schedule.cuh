@@ -1,0 +1,249 @@
+// Balanced split-KV schedule shared by the paged-decode kernels and their merge.
+//
+// Work unit = one visible key token of one (query row, KV head) "segment".  Segment
+// g = ws * Hkv + hkv, where ws = w * S + s indexes the query rows of the paged op.
+// The visible keys of a segment are the concatenation over turns f of the keys
+// l < V_f(ws) = min(L_f, loc[f,ws] + 1) (clipped to the block table), so masked turn
+// padding is never scheduled.  Units are ordered segment-major; with P[ws] the
+// exclusive prefix of V(ws) = sum_f V_f(ws), segment g starts at unit
+// P[ws] * Hkv + hkv * V(ws).  CTA c of n owns units [c*U/n, (c+1)*U/n): every CTA streams
+// the same number of key bytes whatever the sequence lengths are, and a segment is
+// split only where a CTA boundary falls inside it.  A CTA that covers a whole segment
+// writes the final output; the pieces of a split segment go to partial slots
+// (slot 2c for the CTA's first segment, 2c+1 for its last) and are merged by
+// `decode_merge_kernel`.
+//
+// This replaces the reference's uniform split (grid.z = max(2, SMs / (Hkv*W*S)) CTAs
+// striding over every key position, src/kernels/paged_kernel_v21.cuh:385-392).
+#pragma once
+
+#include "common.cuh"
+
+namespace dvb {
+
+struct DecodeSched {
+    long long U;  // total units
+    int n_eff;    // CTAs that own units (<= n_launch)
+    int pad;
+};
+
+// Device-side view of one paged decode call (passed by value).
+struct PagedParams {
+    int F, W, Hq, Hkv, E, S, R, BS, maxb, WS, gqa, cap;
+    long long NB;
+    float scale_log2;  // scale * log2(e)
+    void* out;
+    const void* q;
+    const float* cos;
+    const float* sin;
+    const int* loc;
+    const int* L;
+    const void* k;
+    const void* v;
+    const int* bt;
+    float* lse_out;
+    float* out_f32;
+    DecodeSched* sched;
+    long long* P;      // [WS + 1]
+    float* part_o;     // [n_launch * 2][16][E]
+    float* part_lse;   // [n_launch * 2][16]
+    int n_launch;
+    int min_units;
+    // varlen: query row ws is packed token t (S == 1); its block-table row is the
+    // sequence containing t, found once by the prep kernel from cu_seqlens_q.
+    const int* cu_q;   // [nseq + 1] or null (decode: block-table row = ws / S)
+    int nseq;
+    int* row_seq;      // [WS] workspace, valid when cu_q != null
+    int cs_stride;     // floats per cos/sin row: R (decode) or R/2 (varlen)
+};
+
+__device__ __forceinline__ int row_block_table(const PagedParams& p, int ws) {
+    return p.cu_q ? p.row_seq[ws] : ws / p.S;
+}
+
+// Visible keys of turn f (offset `off` in the sequence's logical cache) for a query with
+// location `loc`: l < L, l <= loc, and off + l inside the block table (`cap` positions).
+__device__ __forceinline__ int turn_vis(int L, int loc, int off, int cap) {
+    int v = min(L, loc + 1);
+    v = min(v, cap - off);
+    return v > 0 ? v : 0;
+}
+
+__device__ __forceinline__ int seg_visible(const PagedParams& p, int ws) {
+    int off = 0, tot = 0;
+    for (int f = 0; f < p.F; ++f) {
+        int L = __ldg(p.L + f);
+        tot += turn_vis(L, __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap);
+        off += L;
+    }
+    return tot;
+}
+
+__device__ __forceinline__ long long cta_start(long long c, long long U, int n) { return c * U / n; }
+
+// CTA whose unit range contains u (ranges are non-empty because U >= n).
+__device__ __forceinline__ int cta_of(long long u, long long U, int n) {
+    int c = (int)(u * n / U);
+    if (c + 1 < n && cta_start(c + 1, U, n) <= u) ++c;
+    return c;
+}
+
+// One pass over the schedule: fills P and the header.  Single CTA of 1024 threads.
+__global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
+    __shared__ long long warp_tot[32];
+    __shared__ long long carry_s;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    if (tid == 0) carry_s = 0;
+    __syncthreads();
+    for (int base = 0; base < p.WS; base += 1024) {
+        const int ws = base + tid;
+        long long v = ws < p.WS ? (long long)seg_visible(p, ws) : 0;
+        // inclusive warp scan
+        long long x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            long long y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) warp_tot[wid] = x;
+        __syncthreads();
+        if (wid == 0) {
+            long long t = warp_tot[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                long long y = __shfl_up_sync(0xffffffffu, t, o);
+                if (lane >= o) t += y;
+            }
+            warp_tot[lane] = t;  // inclusive prefix of warp totals
+        }
+        __syncthreads();
+        const long long carry = carry_s;
+        const long long excl = carry + (wid ? warp_tot[wid - 1] : 0) + x - v;
+        if (ws < p.WS) p.P[ws] = excl;
+        __syncthreads();
+        if (tid == 1023) carry_s = excl + v;
+        __syncthreads();
+    }
+    if (p.cu_q) {
+        // sequence of each packed token: the first w with t < cu[w+1]
+        // (src/kernels/varlen_paged_kernel_v21.cuh:40-47), 0 if there is none.
+        for (int t = tid; t < p.WS; t += 1024) {
+            int lo = 0, hi = p.nseq;  // search in [lo, hi)
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (t < __ldg(p.cu_q + mid + 1)) hi = mid; else lo = mid + 1;
+            }
+            p.row_seq[t] = lo < p.nseq ? lo : 0;
+        }
+    }
+    if (tid == 0) {
+        const long long tot = carry_s;
+        p.P[p.WS] = tot;
+        const long long U = tot * p.Hkv;
+        long long want = (U + p.min_units - 1) / p.min_units;
+        int n = (int)(want < p.n_launch ? want : p.n_launch);
+        p.sched->U = U;
+        p.sched->n_eff = U > 0 ? (n > 0 ? n : 1) : 0;
+    }
+}
+
+// Walks the tiles of one CTA's unit range in order.  Each tile lies inside one turn of
+// one segment and holds at most TILE keys.  Producer (loads) and consumer (math) each
+// run their own copy in lock step.
+struct TileDesc {
+    int ws, hkv, f, pos0, n;
+    bool new_seg, new_turn, seg_last, seg_complete, first_piece;
+};
+
+template <int TILE> struct TileIter {
+    int ws, hkv, f, t, off, vis;
+    long long rem;
+    int seg_left;
+    bool from_start, pend_seg, pend_turn, first_seg;
+
+    __device__ __forceinline__ int seg_len(const PagedParams& p, int w) const {
+        return (int)(p.P[w + 1] - p.P[w]);
+    }
+
+    // ws0: segment row containing u0 (found by the caller); u0/u1: unit range.
+    __device__ __forceinline__ void init(const PagedParams& p, int ws0, long long u0, long long u1) {
+        ws = ws0;
+        const int V = seg_len(p, ws);
+        long long r = u0 - p.P[ws] * p.Hkv;
+        hkv = (int)(r / V);
+        int ts = (int)(r - (long long)hkv * V);
+        seg_left = V - ts;
+        from_start = (ts == 0);
+        f = 0;
+        off = 0;
+        vis = turn_vis(__ldg(p.L), __ldg(p.loc + ws), 0, p.cap);
+        while (ts >= vis) {
+            ts -= vis;
+            off += __ldg(p.L + f);
+            ++f;
+            vis = turn_vis(__ldg(p.L + f), __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap);
+        }
+        t = ts;
+        rem = u1 - u0;
+        pend_seg = pend_turn = true;
+        first_seg = true;
+    }
+
+    __device__ __forceinline__ bool next(const PagedParams& p, TileDesc& d) {
+        if (rem <= 0) return false;
+        while (t >= vis) {
+            off += __ldg(p.L + f);
+            ++f;
+            t = 0;
+            pend_turn = true;
+            if (f == p.F) {
+                f = 0;
+                off = 0;
+                if (++hkv == p.Hkv) {
+                    hkv = 0;
+                    do { ++ws; } while (p.P[ws + 1] == p.P[ws]);
+                }
+                seg_left = seg_len(p, ws);
+                from_start = true;
+                pend_seg = true;
+                first_seg = false;
+            }
+            vis = turn_vis(__ldg(p.L + f), __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap);
+        }
+        int n = vis - t;
+        if (n > TILE) n = TILE;
+        if ((long long)n > rem) n = (int)rem;
+        d.ws = ws;
+        d.hkv = hkv;
+        d.f = f;
+        d.pos0 = off + t;
+        d.n = n;
+        d.new_seg = pend_seg;
+        d.new_turn = pend_turn;
+        d.first_piece = first_seg;
+        t += n;
+        rem -= n;
+        seg_left -= n;
+        d.seg_last = (seg_left == 0) || (rem == 0);
+        d.seg_complete = from_start && (seg_left == 0);
+        pend_seg = pend_turn = false;
+        return true;
+    }
+};
+
+// Segment row containing unit u0: the largest ws with P[ws] * Hkv <= u0 (so empty rows
+// before a non-empty one are skipped).  Block-wide; all threads get the result.
+template <int NT>
+__device__ __forceinline__ int find_row(const PagedParams& p, long long u0) {
+    int cnt = 0;
+    for (int base = 0; base < p.WS; base += NT) {
+        const int i = base + (int)threadIdx.x;
+        const int pred = (i < p.WS) && (p.P[i] * p.Hkv <= u0);
+        const int c = __syncthreads_count(pred);
+        cnt += c;
+        if (c < NT) break;
+    }
+    return cnt - 1;
+}
+
+}  // namespace dvb

@@ -1,0 +1,366 @@
+// torch.ops.libdvatt.* registration for the B200 build: the schemas of the reference
+// extension (src/binding.cu:407-430), implemented on top of the C ABI in
+// libdvattn_b200.so.  Shapes are read and checked here exactly as the reference reads
+// them; the kernels run on the current torch stream of the output's device, and the
+// split-KV workspace comes from the torch caching allocator (no process-wide statics).
+#include <ATen/ATen.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+#include <torch/library.h>
+
+#include <vector>
+
+#include "../../include/dvattn_b200.h"
+
+namespace {
+
+int dtype_code(const at::Tensor& t) {
+    switch (t.scalar_type()) {
+        case at::kFloat: return DVATTN_FLOAT32;
+        case at::kHalf: return DVATTN_FLOAT16;
+        case at::kBFloat16: return DVATTN_BFLOAT16;
+        default:
+            // The reference silently does nothing for other dtypes (src/binding.cu:318-324).
+            TORCH_CHECK(false, "dvattn: unsupported dtype ", t.scalar_type(), " (float32, float16 or bfloat16)");
+    }
+}
+
+void check_status(int st, const char* what) {
+    TORCH_CHECK(st == DVATTN_OK, "dvattn: ", what, " failed: ", dvattn_status_string(st));
+}
+
+void check_cuda_tensor(const at::Tensor& t, const char* name, const at::Tensor& out) {
+    TORCH_CHECK(t.is_cuda(), "dvattn: ", name, " must be a CUDA tensor");
+    TORCH_CHECK(t.device() == out.device(), "dvattn: ", name, " is on ", t.device(), " but output is on ", out.device());
+    TORCH_CHECK(t.is_contiguous(), "dvattn: ", name, " must be contiguous");
+}
+
+using Named = std::pair<const at::Tensor*, const char*>;
+void check_all(const at::Tensor& out, std::initializer_list<Named> ts) {
+    for (const Named& n : ts) check_cuda_tensor(*n.first, n.second, out);
+}
+
+void check_i32(const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.scalar_type() == at::kInt, "dvattn: ", name, " must be int32");
+}
+
+dvattn_stream_t cur_stream(const at::Tensor& out) {
+    return reinterpret_cast<dvattn_stream_t>(at::cuda::getCurrentCUDAStream(out.device().index()).stream());
+}
+
+// ---------------------------------------------------------------------------------
+// dvattn_paged_sdpa (src/binding.cu:151-203 / 312-325)
+// ---------------------------------------------------------------------------------
+void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& fragment_lengths,
+                const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& block_tables,
+                const c10::optional<at::Tensor>& lse, const c10::optional<at::Tensor>& out_f32) {
+    const c10::cuda::CUDAGuard guard(out.device());
+    const int dt = dtype_code(out);
+    TORCH_CHECK(out.dim() == 4, "dvattn_paged_sdpa: output must be [W, Hq, S, Ev]");
+    TORCH_CHECK(queries.dim() == 4 && locations.dim() == 3 && cosines.dim() == 4 && sines.dim() == 4 &&
+                    k_cache.dim() == 4 && v_cache.dim() == 4 && block_tables.dim() == 2 && fragment_lengths.dim() == 1,
+                "dvattn_paged_sdpa: wrong tensor ranks");
+    for (auto* pr : {&queries, &k_cache, &v_cache})
+        TORCH_CHECK(pr->scalar_type() == out.scalar_type(), "dvattn_paged_sdpa: queries/k_cache/v_cache must have the output dtype");
+    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat,
+                "dvattn_paged_sdpa: cosines/sines must be float32");
+    check_i32(locations, "locations");
+    check_i32(fragment_lengths, "fragment_lengths");
+    check_i32(block_tables, "block_tables");
+    check_cuda_tensor(out, "output", out);
+    check_cuda_tensor(queries, "queries", out);
+    check_cuda_tensor(locations, "locations", out);
+    check_cuda_tensor(cosines, "cosines", out);
+    check_cuda_tensor(sines, "sines", out);
+    check_cuda_tensor(fragment_lengths, "fragment_lengths", out);
+    check_cuda_tensor(k_cache, "k_cache", out);
+    check_cuda_tensor(v_cache, "v_cache", out);
+    check_cuda_tensor(block_tables, "block_tables", out);
+
+    const int W = out.size(0), Hq = out.size(1), S = out.size(2), Ev = out.size(3);
+    const int F = locations.size(0);
+    TORCH_CHECK(locations.size(1) == W && locations.size(2) == S, "dvattn_paged_sdpa: locations must be [F, W, S]");
+    TORCH_CHECK(queries.size(0) == W && queries.size(1) == Hq && queries.size(2) == S,
+                "dvattn_paged_sdpa: queries must be [W, Hq, S, E]");
+    const int E = queries.size(3);
+    const int R = cosines.size(3);
+    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == W && cosines.size(2) == S, "dvattn_paged_sdpa: cosines must be [F, W, S, R]");
+    TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_paged_sdpa: sines must match cosines");
+    TORCH_CHECK(fragment_lengths.size(0) == F, "dvattn_paged_sdpa: fragment_lengths must be [F]");
+    const int BS = k_cache.size(1), Hkv = k_cache.size(2);
+    TORCH_CHECK(k_cache.size(3) == E, "dvattn_paged_sdpa: k_cache must be [NB, BS, Hkv, E]");
+    TORCH_CHECK(v_cache.size(0) == k_cache.size(0) && v_cache.size(1) == BS && v_cache.size(2) == Hkv && v_cache.size(3) == Ev,
+                "dvattn_paged_sdpa: v_cache must be [NB, BS, Hkv, Ev]");
+    TORCH_CHECK(block_tables.size(0) == W, "dvattn_paged_sdpa: block_tables must be [W, max_blocks]");
+
+    dvattn_paged_args a{};
+    a.dtype = dt;
+    a.F = F; a.W = W; a.Hq = Hq; a.Hkv = Hkv; a.E = E; a.Ev = Ev; a.S = S; a.R = R;
+    a.block_size = BS;
+    a.max_blocks_per_seq = block_tables.size(1);
+    a.num_blocks = k_cache.size(0);
+    a.scale = static_cast<float>(scale);
+    a.out = out.data_ptr();
+    a.queries = queries.const_data_ptr();
+    a.cosines = cosines.const_data_ptr<float>();
+    a.sines = sines.const_data_ptr<float>();
+    a.locations = locations.const_data_ptr<int>();
+    a.fragment_lengths = fragment_lengths.const_data_ptr<int>();
+    a.k_cache = k_cache.const_data_ptr();
+    a.v_cache = v_cache.const_data_ptr();
+    a.block_tables = block_tables.const_data_ptr<int>();
+    if (lse.has_value()) {
+        check_cuda_tensor(*lse, "lse", out);
+        TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() == (int64_t)W * Hq * S, "dvattn: lse must be f32 [W, Hq, S]");
+        a.lse_out = lse->data_ptr<float>();
+    }
+    if (out_f32.has_value()) {
+        check_cuda_tensor(*out_f32, "out_f32", out);
+        TORCH_CHECK(out_f32->scalar_type() == at::kFloat && out_f32->numel() == out.numel(), "dvattn: out_f32 must be f32 like output");
+        a.out_f32 = out_f32->data_ptr<float>();
+    }
+    int st = dvattn_paged_sdpa(&a, nullptr, 0, cur_stream(out));  // validation only when nothing to do
+    if (st == DVATTN_ERR_WORKSPACE) {
+        const size_t wsb = dvattn_paged_sdpa_workspace_size(&a);
+        TORCH_CHECK(wsb > 0, "dvattn_paged_sdpa: could not size the workspace");
+        at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
+        st = dvattn_paged_sdpa(&a, ws.data_ptr(), wsb, cur_stream(out));
+    }
+    check_status(st, "dvattn_paged_sdpa");
+}
+
+void dvattn_paged_sdpa_op(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                          const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& fragment_lengths,
+                          const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& block_tables) {
+    paged_impl(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+               c10::nullopt, c10::nullopt);
+}
+
+void dvattn_paged_sdpa_ex_op(at::Tensor& out, const c10::optional<at::Tensor>& lse,
+                             const c10::optional<at::Tensor>& out_f32, double scale, const at::Tensor& locations,
+                             const at::Tensor& queries, const at::Tensor& cosines, const at::Tensor& sines,
+                             const at::Tensor& fragment_lengths, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                             const at::Tensor& block_tables) {
+    paged_impl(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables, lse,
+               out_f32);
+}
+
+// ---------------------------------------------------------------------------------
+// dvattn_varlen_paged_sdpa (src/binding.cu:249-296 / 327-342)
+// ---------------------------------------------------------------------------------
+void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                 const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& fragment_lengths,
+                 const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& block_tables,
+                 const at::Tensor& cu_seqlens_q, const at::Tensor& cu_seqlens_k, const c10::optional<at::Tensor>& lse,
+                 const c10::optional<at::Tensor>& out_f32) {
+    const c10::cuda::CUDAGuard guard(out.device());
+    const int dt = dtype_code(out);
+    TORCH_CHECK(queries.dim() == 3 && out.dim() == 3 && locations.dim() == 2 && cosines.dim() == 3 && sines.dim() == 3 &&
+                    k_cache.dim() == 4 && v_cache.dim() == 4 && block_tables.dim() == 2 && cu_seqlens_q.dim() == 1,
+                "dvattn_varlen_paged_sdpa: wrong tensor ranks");
+    for (auto* pr : {&queries, &k_cache, &v_cache})
+        TORCH_CHECK(pr->scalar_type() == out.scalar_type(), "dvattn_varlen_paged_sdpa: queries/k_cache/v_cache must have the output dtype");
+    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat,
+                "dvattn_varlen_paged_sdpa: cosines/sines must be float32");
+    check_i32(locations, "locations");
+    check_i32(fragment_lengths, "fragment_lengths");
+    check_i32(block_tables, "block_tables");
+    check_i32(cu_seqlens_q, "cu_seqlens_q");
+    check_all(out, {Named{&queries, "queries"}, Named{&locations, "locations"},
+                    Named{&cosines, "cosines"}, Named{&sines, "sines"},
+                    Named{&fragment_lengths, "fragment_lengths"}, Named{&k_cache, "k_cache"},
+                    Named{&v_cache, "v_cache"}, Named{&block_tables, "block_tables"},
+                    Named{&cu_seqlens_q, "cu_seqlens_q"}, Named{&out, "output"}});
+    (void)cu_seqlens_k;  // accepted and unused, as in the reference
+
+    const int T = queries.size(0), Hq = queries.size(1), E = queries.size(2);
+    const int F = locations.size(0);
+    const int W = cu_seqlens_q.size(0) - 1;
+    const int Ev = v_cache.size(3);
+    TORCH_CHECK(W >= 0, "dvattn_varlen_paged_sdpa: cu_seqlens_q must have W+1 entries");
+    TORCH_CHECK(locations.size(1) == T, "dvattn_varlen_paged_sdpa: locations must be [F, T]");
+    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == T, "dvattn_varlen_paged_sdpa: cosines must be [F, T, R/2]");
+    TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_varlen_paged_sdpa: sines must match cosines");
+    TORCH_CHECK(fragment_lengths.size(0) == F, "dvattn_varlen_paged_sdpa: fragment_lengths must be [F]");
+    TORCH_CHECK(out.size(0) == T && out.size(1) == Hq && out.size(2) == Ev, "dvattn_varlen_paged_sdpa: output must be [T, Hq, Ev]");
+    TORCH_CHECK(k_cache.size(3) == E, "dvattn_varlen_paged_sdpa: k_cache must be [NB, BS, Hkv, E]");
+    TORCH_CHECK(v_cache.size(0) == k_cache.size(0) && v_cache.size(1) == k_cache.size(1) && v_cache.size(2) == k_cache.size(2),
+                "dvattn_varlen_paged_sdpa: v_cache must match k_cache");
+
+    dvattn_varlen_args a{};
+    a.dtype = dt;
+    a.F = F; a.W = W; a.Hq = Hq; a.Hkv = k_cache.size(2); a.E = E; a.Ev = Ev; a.T = T;
+    a.R = cosines.size(2) * 2;
+    a.block_size = k_cache.size(1);
+    a.max_blocks_per_seq = block_tables.size(1);
+    a.num_blocks = k_cache.size(0);
+    a.scale = static_cast<float>(scale);
+    a.out = out.data_ptr();
+    a.queries = queries.const_data_ptr();
+    a.cosines = cosines.const_data_ptr<float>();
+    a.sines = sines.const_data_ptr<float>();
+    a.locations = locations.const_data_ptr<int>();
+    a.fragment_lengths = fragment_lengths.const_data_ptr<int>();
+    a.k_cache = k_cache.const_data_ptr();
+    a.v_cache = v_cache.const_data_ptr();
+    a.block_tables = block_tables.const_data_ptr<int>();
+    a.cu_seqlens_q = cu_seqlens_q.const_data_ptr<int>();
+    a.cu_seqlens_k = nullptr;
+    if (lse.has_value()) {
+        check_cuda_tensor(*lse, "lse", out);
+        TORCH_CHECK(lse->scalar_type() == at::kFloat && lse->numel() == (int64_t)T * Hq, "dvattn: lse must be f32 [T, Hq]");
+        a.lse_out = lse->data_ptr<float>();
+    }
+    if (out_f32.has_value()) {
+        check_cuda_tensor(*out_f32, "out_f32", out);
+        TORCH_CHECK(out_f32->scalar_type() == at::kFloat && out_f32->numel() == out.numel(), "dvattn: out_f32 must be f32 like output");
+        a.out_f32 = out_f32->data_ptr<float>();
+    }
+    int st = dvattn_varlen_paged_sdpa(&a, nullptr, 0, cur_stream(out));
+    if (st == DVATTN_ERR_WORKSPACE) {
+        const size_t wsb = dvattn_varlen_paged_sdpa_workspace_size(&a);
+        TORCH_CHECK(wsb > 0, "dvattn_varlen_paged_sdpa: could not size the workspace");
+        at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
+        st = dvattn_varlen_paged_sdpa(&a, ws.data_ptr(), wsb, cur_stream(out));
+    }
+    check_status(st, "dvattn_varlen_paged_sdpa");
+}
+
+void dvattn_varlen_paged_sdpa_op(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                                 const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& fragment_lengths,
+                                 const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& block_tables,
+                                 const at::Tensor& cu_seqlens_q, const at::Tensor& cu_seqlens_k) {
+    varlen_impl(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+                cu_seqlens_q, cu_seqlens_k, c10::nullopt, c10::nullopt);
+}
+
+void dvattn_varlen_paged_sdpa_ex_op(at::Tensor& out, const c10::optional<at::Tensor>& lse,
+                                    const c10::optional<at::Tensor>& out_f32, double scale,
+                                    const at::Tensor& locations, const at::Tensor& queries, const at::Tensor& cosines,
+                                    const at::Tensor& sines, const at::Tensor& fragment_lengths,
+                                    const at::Tensor& k_cache, const at::Tensor& v_cache,
+                                    const at::Tensor& block_tables, const at::Tensor& cu_seqlens_q,
+                                    const at::Tensor& cu_seqlens_k) {
+    varlen_impl(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+                cu_seqlens_q, cu_seqlens_k, lse, out_f32);
+}
+
+// ---------------------------------------------------------------------------------
+// dvattn_rope / dvattn_varlen_rope (src/binding.cu:41-77, 205-247)
+// ---------------------------------------------------------------------------------
+void dvattn_rope_op(at::Tensor& out, const at::Tensor& queries, const at::Tensor& cosines, const at::Tensor& sines) {
+    const c10::cuda::CUDAGuard guard(out.device());
+    const int dt = dtype_code(out);
+    TORCH_CHECK(out.dim() == 5 && queries.dim() == 4 && cosines.dim() == 4 && sines.dim() == 4, "dvattn_rope: wrong tensor ranks");
+    TORCH_CHECK(queries.scalar_type() == out.scalar_type(), "dvattn_rope: queries must have the output dtype");
+    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat, "dvattn_rope: cosines/sines must be float32");
+    check_all(out, {Named{&queries, "queries"}, Named{&cosines, "cosines"},
+                    Named{&sines, "sines"}, Named{&out, "output"}});
+    const int F = out.size(0), W = out.size(1), Hq = out.size(2), S = out.size(3), E = out.size(4);
+    const int R = cosines.size(3);
+    TORCH_CHECK(queries.size(0) == W && queries.size(1) == Hq && queries.size(2) == S && queries.size(3) == E,
+                "dvattn_rope: queries must be [W, Hq, S, E]");
+    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == W && cosines.size(2) == S, "dvattn_rope: cosines must be [F, W, S, R]");
+    TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_rope: sines must match cosines");
+    check_status(dvattn_rope(dt, F, W, Hq, S, E, R, out.data_ptr(), queries.const_data_ptr(),
+                             cosines.const_data_ptr<float>(), sines.const_data_ptr<float>(), cur_stream(out)),
+                 "dvattn_rope");
+}
+
+void dvattn_varlen_rope_op(at::Tensor& out, const at::Tensor& queries, const at::Tensor& cosines, const at::Tensor& sines) {
+    const c10::cuda::CUDAGuard guard(out.device());
+    const int dt = dtype_code(out);
+    TORCH_CHECK(out.dim() == 4 && queries.dim() == 3 && cosines.dim() == 3 && sines.dim() == 3, "dvattn_varlen_rope: wrong tensor ranks");
+    TORCH_CHECK(queries.scalar_type() == out.scalar_type(), "dvattn_varlen_rope: queries must have the output dtype");
+    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat, "dvattn_varlen_rope: cosines/sines must be float32");
+    check_all(out, {Named{&queries, "queries"}, Named{&cosines, "cosines"},
+                    Named{&sines, "sines"}, Named{&out, "output"}});
+    const int F = out.size(0), T = out.size(1), H = out.size(2), E = out.size(3);
+    const int R = cosines.size(2) * 2;
+    TORCH_CHECK(queries.size(0) == T && queries.size(1) == H && queries.size(2) == E, "dvattn_varlen_rope: queries must be [T, H, E]");
+    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == T, "dvattn_varlen_rope: cosines must be [F, T, R/2]");
+    TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_varlen_rope: sines must match cosines");
+    check_status(dvattn_varlen_rope(dt, F, T, H, E, R, out.data_ptr(), queries.const_data_ptr(),
+                                    cosines.const_data_ptr<float>(), sines.const_data_ptr<float>(), cur_stream(out)),
+                 "dvattn_varlen_rope");
+}
+
+// ---------------------------------------------------------------------------------
+// LSE merge of per-GPU partials (no reference counterpart as a public op)
+// ---------------------------------------------------------------------------------
+void dvattn_lse_merge_op(at::Tensor& out, const c10::optional<at::Tensor>& lse_out, const at::Tensor& part_out,
+                         const at::Tensor& part_lse) {
+    const c10::cuda::CUDAGuard guard(out.device());
+    const int dt = dtype_code(out);
+    TORCH_CHECK(part_out.scalar_type() == at::kFloat && part_lse.scalar_type() == at::kFloat, "dvattn_lse_merge: partials must be float32");
+    check_cuda_tensor(part_out, "part_out", out);
+    check_cuda_tensor(part_lse, "part_lse", out);
+    check_cuda_tensor(out, "output", out);
+    TORCH_CHECK(part_out.dim() >= 2, "dvattn_lse_merge: part_out must be [parts, ..., Ev]");
+    const int parts = part_out.size(0);
+    const int Ev = part_out.size(-1);
+    const int64_t rows = out.numel() / Ev;
+    TORCH_CHECK(part_out.numel() == (int64_t)parts * rows * Ev && part_lse.numel() == (int64_t)parts * rows,
+                "dvattn_lse_merge: part_out [parts, rows.., Ev] / part_lse [parts, rows..] do not match output");
+    float* lp = nullptr;
+    if (lse_out.has_value()) {
+        check_cuda_tensor(*lse_out, "lse_out", out);
+        TORCH_CHECK(lse_out->scalar_type() == at::kFloat && lse_out->numel() == rows, "dvattn_lse_merge: lse_out must be f32 [rows]");
+        lp = lse_out->data_ptr<float>();
+    }
+    check_status(dvattn_lse_merge(dt, parts, rows, Ev, part_out.const_data_ptr<float>(), part_lse.const_data_ptr<float>(),
+                                  out.data_ptr(), lp, cur_stream(out)),
+                 "dvattn_lse_merge");
+}
+
+// The contiguous-fragment ops exist in the schema set but are not built for B200.
+void not_built(const char* name) {
+    TORCH_CHECK(false, "dvattn: ", name,
+                " (contiguous-fragment attention) is not part of the B200 build; use dvattn_paged_sdpa over a paged cache");
+}
+void dvattn_sdpa_op(at::Tensor&, double, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                    const std::vector<at::Tensor>&, const std::vector<at::Tensor>&) {
+    not_built("dvattn_sdpa");
+}
+void dvattn_fused_op(at::Tensor&, at::Tensor&, double, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                     const std::vector<at::Tensor>&, const std::vector<at::Tensor>&, const at::Tensor&, const at::Tensor&) {
+    not_built("dvattn_fused");
+}
+
+}  // namespace
+
+TORCH_LIBRARY(libdvatt, m) {
+    std::vector<at::Tag> tags{at::Tag::needs_fixed_stride_order};
+    m.def("dvattn_sdpa(Tensor(a!) output, float scale, Tensor locations, Tensor queries, "
+          "Tensor fragment_lengths, Tensor[] key_fragments, Tensor[] value_fragments) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_paged_sdpa(Tensor(a!) output, float scale, Tensor locations, Tensor queries, "
+          "Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, Tensor v_cache, Tensor block_tables) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_rope(Tensor(a!) output, Tensor queries, Tensor cosines, Tensor sines) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_fused(Tensor(a!) output, Tensor(b!) rq, float scale, Tensor locations, Tensor queries, "
+          "Tensor fragment_lengths, Tensor[] key_fragments, Tensor[] value_fragments, Tensor cosines, Tensor sines) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_varlen_rope(Tensor(a!) output, Tensor queries, Tensor cosines, Tensor sines) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_varlen_paged_sdpa(Tensor(a!) output, float scale, Tensor locations, Tensor queries, "
+          "Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, Tensor v_cache, "
+          "Tensor block_tables, Tensor cu_seqlens_q, Tensor cu_seqlens_k) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    // B200 additions: optional natural-log LSE and f32 output (for cross-GPU merges), and the merge itself.
+    m.def("dvattn_paged_sdpa_ex(Tensor(a!) output, Tensor(b!)? lse, Tensor(c!)? out_f32, float scale, Tensor locations, "
+          "Tensor queries, Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, Tensor v_cache, "
+          "Tensor block_tables) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_varlen_paged_sdpa_ex(Tensor(a!) output, Tensor(b!)? lse, Tensor(c!)? out_f32, float scale, "
+          "Tensor locations, Tensor queries, Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, "
+          "Tensor v_cache, Tensor block_tables, Tensor cu_seqlens_q, Tensor cu_seqlens_k) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_lse_merge(Tensor(a!) output, Tensor(b!)? lse_out, Tensor part_out, Tensor part_lse) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+}
+
+TORCH_LIBRARY_IMPL(libdvatt, CUDA, m) {
+    m.impl("dvattn_sdpa", dvattn_sdpa_op);
+    m.impl("dvattn_paged_sdpa", dvattn_paged_sdpa_op);
+    m.impl("dvattn_rope", dvattn_rope_op);
+    m.impl("dvattn_fused", dvattn_fused_op);
+    m.impl("dvattn_varlen_rope", dvattn_varlen_rope_op);
+    m.impl("dvattn_varlen_paged_sdpa", dvattn_varlen_paged_sdpa_op);
+    m.impl("dvattn_paged_sdpa_ex", dvattn_paged_sdpa_ex_op);
+    m.impl("dvattn_varlen_paged_sdpa_ex", dvattn_varlen_paged_sdpa_ex_op);
+    m.impl("dvattn_lse_merge", dvattn_lse_merge_op);
+}

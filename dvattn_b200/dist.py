@@ -1,0 +1,89 @@
+"""Multi-GPU partitioning of the paged decode (one process per GPU, torch.distributed).
+
+Two ways the work splits across the GPUs of one box:
+
+* by sequence (batch decode, varlen prefill): sequences are independent, so each rank
+  runs the op on its own sequences with no data-path collective.  ``balance`` assigns
+  sequences to ranks by longest-processing-time on their attended-key counts.
+* by KV chunk (one very long context): each rank holds a page-aligned slice of every
+  sequence's positions, runs the op on its slice with LSE output, and the partial
+  outputs are exchanged over NCCL (all-gather of f32 O and LSE) and merged by the
+  ``dvattn_lse_merge`` kernel -- the same log-sum-exp reduction the single-GPU split-KV
+  uses (src/kernels/paged_kernel_v21.cuh:307-374), one level up.
+
+The reference has no multi-GPU path; it would have to run one process per GPU because
+its workspace is a process-wide static (src/kernels/paged_kernel_v21.cuh:397-408).
+"""
+from __future__ import annotations
+
+import heapq
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .workloads import PagedCase
+
+
+def balance(weights: Sequence[int], n: int) -> List[List[int]]:
+    """Longest-processing-time assignment of items (by weight) to n bins; each bin's item
+    list is sorted.  Deterministic (ties broken by index)."""
+    heap = [(0, r) for r in range(n)]
+    bins: List[List[int]] = [[] for _ in range(n)]
+    for i in sorted(range(len(weights)), key=lambda i: (-weights[i], i)):
+        load, r = heapq.heappop(heap)
+        bins[r].append(i)
+        heapq.heappush(heap, (load + int(weights[i]), r))
+    return [sorted(b) for b in bins]
+
+
+def kv_chunk_bounds(total: int, block_size: int, n: int) -> List[Tuple[int, int]]:
+    """Split logical positions [0, total) into n page-aligned, contiguous, near-equal chunks."""
+    pages = -(-total // block_size)
+    out = []
+    for r in range(n):
+        a = pages * r // n * block_size
+        b = min(total, pages * (r + 1) // n * block_size)
+        out.append((min(a, total), b))
+    return out
+
+
+def kv_chunk_shard(case: PagedCase, rank: int, world: int) -> PagedCase:
+    """The slice of a single-turn paged case that rank `rank` of `world` attends over.
+    Keys keep their rotation (it is relative to the turn start, which does not move);
+    locations shift by the chunk start, so key l of the chunk is visible iff
+    a + l <= loc.  The page pool is shared (views)."""
+    F = case.locations.size(0)
+    if F != 1:
+        raise ValueError("kv_chunk_shard: KV-chunk sharding is defined for single-turn caches")
+    BS = case.k_cache.size(1)
+    L = int(case.fragment_lengths[0].item())
+    a, b = kv_chunk_bounds(L, BS, world)[rank]
+    dev = case.locations.device
+    loc = case.locations.to(torch.int64) - a
+    loc = torch.clamp(loc, min=-1).to(torch.int32)
+    bt = case.block_tables[:, a // BS: max(a // BS + 1, -(-b // BS))].contiguous()
+    return PagedCase(queries=case.queries, locations=loc.contiguous(), cosines=case.cosines, sines=case.sines,
+                     fragment_lengths=torch.tensor([b - a], dtype=torch.int32, device=dev), k_cache=case.k_cache,
+                     v_cache=case.v_cache, block_tables=bt, scale=case.scale, turn_lens=case.turn_lens,
+                     meta=dict(case.meta, chunk=(a, b)))
+
+
+def _cuda_merge(part_out: torch.Tensor, part_lse: torch.Tensor, out: torch.Tensor, lse: Optional[torch.Tensor]):
+    from .api import dvattn_lse_merge
+    dvattn_lse_merge(part_out, part_lse, out, lse)
+    return out
+
+
+def allgather_merge(out_f32: torch.Tensor, lse: torch.Tensor, out: torch.Tensor, group=None,
+                    merge: Optional[Callable] = None, lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Exchange this rank's partial (f32 output [..., Ev] + natural-log LSE [...]) with
+    every rank of `group` and merge them into `out` on every rank.  `merge` defaults to
+    the CUDA merge kernel; it is injectable so the exchange logic can run on CPU ranks."""
+    world = dist.get_world_size(group)
+    po = [torch.empty_like(out_f32) for _ in range(world)]
+    pl = [torch.empty_like(lse) for _ in range(world)]
+    dist.all_gather(po, out_f32.contiguous(), group=group)
+    dist.all_gather(pl, lse.contiguous(), group=group)
+    po, pl = torch.stack(po), torch.stack(pl)
+    return (merge or _cuda_merge)(po, pl, out, lse_out)

@@ -1,0 +1,183 @@
+/*
+ * dvattn_b200.h -- C ABI of the B200 (sm_100a) DVAttn attention forward.
+ *
+ * Plain pointers and sizes only: no torch or C++ types cross this boundary, so the
+ * library can be bound from ctypes, cgo, JNI or a C++ engine.  Every entry point is
+ * asynchronous on the given stream and returns a status code (DVATTN_OK == 0).
+ *
+ * Tensor layouts (all row-major, contiguous; T = the args' dtype):
+ *   paged decode   queries [W,Hq,S,E] T, cosines/sines [F,W,S,R] f32 (only the first
+ *                  R/2 entries of each row are read), locations [F,W,S] i32,
+ *                  fragment_lengths [F] i32, k_cache [NB,BS,Hkv,E] T,
+ *                  v_cache [NB,BS,Hkv,Ev] T, block_tables [W,max_blocks] i32,
+ *                  out [W,Hq,S,Ev] T.
+ *   varlen prefill queries [T,Hq,E] T, cosines/sines [F,T,R/2] f32, locations [F,T] i32,
+ *                  cu_seqlens_q [W+1] i32, out [T,Hq,Ev] T.
+ * Semantics: cache turn f occupies logical positions [sum_{f'<f} L_f', +L_f) of each
+ * sequence's block table; key l of turn f is visible to a query iff l <= loc[f,.] and
+ * l < L_f; the query is rotated per turn by that turn's cos/sin (NeoX rotate-half
+ * pairing (e, e+R/2) for e < R/2, dims >= R pass through) and rounded to T first.
+ * A query row that sees no key at all gets an output of zeros.
+ */
+#ifndef DVATTN_B200_H
+#define DVATTN_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same handle type as cudaStream_t (a CUstream_st*); NULL = legacy default stream. */
+typedef struct CUstream_st* dvattn_stream_t;
+
+/* Status codes. */
+#define DVATTN_OK 0
+#define DVATTN_ERR_INVALID_ARGUMENT 1 /* null pointer, negative or inconsistent size      */
+#define DVATTN_ERR_UNSUPPORTED 2      /* dtype / head dim / GQA ratio outside the kernels */
+#define DVATTN_ERR_WORKSPACE 3        /* workspace missing, too small or misaligned        */
+#define DVATTN_ERR_CUDA 4             /* a CUDA runtime call or kernel launch failed       */
+
+/* Element types (the dtype of queries, caches and output; cos/sin are always f32). */
+#define DVATTN_FLOAT32 0
+#define DVATTN_FLOAT16 1
+#define DVATTN_BFLOAT16 2
+
+/*
+ * Arguments of one paged decode call.  Mirrors `Shape` (src/common.h:5-20) plus the
+ * tensors of the `dvattn_paged_sdpa` schema (src/binding.cu:412-413, 151-203).
+ */
+typedef struct dvattn_paged_args {
+    int dtype;                    /* DVATTN_FLOAT32 / FLOAT16 / BFLOAT16                 */
+    int F, W, Hq, Hkv, E, Ev, S;  /* turns, sequences, heads, head dims, queries/seq     */
+    int R;                        /* rotary dim = cosines.size(3); even, 0 <= R <= E     */
+    int block_size;               /* tokens per page (k_cache.size(1))                  */
+    int max_blocks_per_seq;       /* block_tables.size(1)                               */
+    long long num_blocks;         /* k_cache.size(0); pages outside [0,NB) are not read  */
+    float scale;                  /* softmax scale applied to q.k                        */
+    void* out;
+    const void* queries;
+    const float* cosines;
+    const float* sines;
+    const int* locations;
+    const int* fragment_lengths;
+    const void* k_cache;
+    const void* v_cache;
+    const int* block_tables;
+    float* lse_out;               /* optional [W,Hq,S] natural-log LSE of scale*q.k      */
+    float* out_f32;               /* optional [W,Hq,S,Ev] f32 copy of the output        */
+} dvattn_paged_args;
+
+/*
+ * Arguments of one varlen (packed, chunked-prefill) call.  Mirrors the
+ * `dvattn_varlen_paged_sdpa` schema (src/binding.cu:418-420, 249-296).
+ */
+typedef struct dvattn_varlen_args {
+    int dtype;
+    int F, W, Hq, Hkv, E, Ev;     /* W = number of sequences = cu_seqlens_q.size(0)-1   */
+    int T;                        /* total packed query tokens                          */
+    int R;                        /* rotary dim = 2 * cosines.size(2)                   */
+    int block_size;
+    int max_blocks_per_seq;
+    long long num_blocks;
+    float scale;
+    void* out;
+    const void* queries;
+    const float* cosines;
+    const float* sines;
+    const int* locations;
+    const int* fragment_lengths;
+    const void* k_cache;
+    const void* v_cache;
+    const int* block_tables;
+    const int* cu_seqlens_q;      /* [W+1] packed query offsets                          */
+    const int* cu_seqlens_k;      /* [W+1] accepted, unused (as in the reference)        */
+    float* lse_out;               /* optional [T,Hq] natural-log LSE                     */
+    float* out_f32;               /* optional [T,Hq,Ev] f32 copy of the output          */
+} dvattn_varlen_args;
+
+/* ABI version of this header (bumped on any layout change of the structs above). */
+int dvattn_abi_version(void);
+
+/* Human-readable name of a status code. */
+const char* dvattn_status_string(int status);
+
+/*
+ * Bytes of device workspace `dvattn_paged_sdpa` needs for these arguments on the
+ * current device (split-KV partials, per-sequence prefix sums).  Replaces the
+ * function-static workspace of paged_v21::dvattn_paged_attention_gpu
+ * (src/kernels/paged_kernel_v21.cuh:397-408).  Returns 0 when the arguments are invalid.
+ */
+size_t dvattn_paged_sdpa_workspace_size(const dvattn_paged_args* args);
+
+/*
+ * Paged decode: rotate q per turn (fused), attend over the paged cache, merge split-KV
+ * partials.  Replaces dvattn_paged_attention_tpl + rope_gpu + paged_v21::
+ * dvattn_paged_attention_gpu (src/binding.cu:151-203, src/rope.cuh:2-65,
+ * src/kernels/paged_kernel_v21.cuh:377-431).  `workspace` is caller-owned device
+ * memory of at least dvattn_paged_sdpa_workspace_size() bytes, 256-byte aligned; it
+ * need not be zeroed.  Calls on the same workspace must be stream-ordered.
+ */
+int dvattn_paged_sdpa(const dvattn_paged_args* args, void* workspace, size_t workspace_bytes,
+                      dvattn_stream_t stream);
+
+/* Phases of dvattn_paged_sdpa (all three run on one stream, in this order). */
+#define DVATTN_PHASE_ALL 0
+#define DVATTN_PHASE_SCHEDULE 1 /* visible-key prefix sums and the per-CTA work split   */
+#define DVATTN_PHASE_ATTEND 2   /* the split-KV attention kernel (the HBM stream)       */
+#define DVATTN_PHASE_MERGE 3    /* log-sum-exp merge of segments split across CTAs      */
+
+/*
+ * One phase of dvattn_paged_sdpa on the same arguments and workspace; running SCHEDULE,
+ * ATTEND, MERGE in order is exactly dvattn_paged_sdpa (PHASE_ALL).  Lets a caller put
+ * events or other work between the phases (e.g. timing the attention kernel alone).
+ * No reference counterpart: the reference launches its kernels back to back inside
+ * paged_v21::dvattn_paged_attention_gpu (src/kernels/paged_kernel_v21.cuh:408-425).
+ */
+int dvattn_paged_sdpa_phase(const dvattn_paged_args* args, void* workspace, size_t workspace_bytes, int phase,
+                            dvattn_stream_t stream);
+
+/* Workspace bytes of dvattn_varlen_paged_sdpa (see dvattn_paged_sdpa_workspace_size). */
+size_t dvattn_varlen_paged_sdpa_workspace_size(const dvattn_varlen_args* args);
+
+/*
+ * Varlen chunked prefill over the paged cache.  Replaces dvattn_varlen_paged_attention_tpl
+ * + rope_varlen_gpu + varlen_paged_v21::dvattn_varlen_paged_attention_gpu
+ * (src/binding.cu:249-296, src/rope.cuh:67-114, src/kernels/varlen_paged_kernel_v21.cuh:373-428).
+ * A turn whose location is negative for a token is skipped for that token.
+ */
+int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace,
+                             size_t workspace_bytes, dvattn_stream_t stream);
+
+/*
+ * Standalone query rotation, schema `dvattn_rope` (src/binding.cu:41-77, src/rope.cuh:2-65):
+ * out [F,W,Hq,S,E] T = rotate(queries [W,Hq,S,E] T, cos/sin [F,W,S,R] f32).
+ */
+int dvattn_rope(int dtype, int F, int W, int Hq, int S, int E, int R, void* out,
+                const void* queries, const float* cosines, const float* sines,
+                dvattn_stream_t stream);
+
+/*
+ * Standalone varlen query rotation, schema `dvattn_varlen_rope` (src/binding.cu:205-247,
+ * src/rope.cuh:67-114): out [F,T,H,E] T from queries [T,H,E] and cos/sin [F,T,R/2] f32.
+ */
+int dvattn_varlen_rope(int dtype, int F, int T, int H, int E, int R, void* out,
+                       const void* queries, const float* cosines, const float* sines,
+                       dvattn_stream_t stream);
+
+/*
+ * Log-sum-exp merge of `num_parts` partial attention results over disjoint key sets
+ * (the split-KV reduce of src/kernels/paged_kernel_v21.cuh:307-374, exposed so that
+ * partials gathered from several GPUs can be merged):
+ *   part_out [num_parts][rows][Ev] f32 (each normalised), part_lse [num_parts][rows]
+ *   natural-log LSE (-inf = empty part)  ->  out [rows][Ev] T, optional lse_out [rows].
+ * Rows whose parts are all empty get zeros.
+ */
+int dvattn_lse_merge(int dtype, int num_parts, long long rows, int Ev, const float* part_out,
+                     const float* part_lse, void* out, float* lse_out, dvattn_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DVATTN_B200_H */
