@@ -10,6 +10,9 @@
 #include "decode.cuh"
 #include "schedule.cuh"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 namespace dvb {
 
 // ----------------------------------------------------------------------------------
@@ -312,6 +315,387 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
 }
 
 // ==================================================================================
+// TMA kernel (f16 / bf16, page sizes that tile 64-key windows): warp-specialised.
+// Warp 4 (producer) walks the schedule, looks the window's pages up in the block table
+// and issues one 3-D TMA box per (page, 64-column panel, K|V) into a stage of the ring;
+// the stage's full mbarrier counts the bytes.  Warps 0-3 (consumers) each take 16 keys
+// of the 64-key window: ldmatrix + mma.sync for S = Q K^T and O += P V, online softmax,
+// then release the stage on its empty mbarrier.  Keys of a window outside the tile's
+// visible range are masked (-inf scores) and their V rows are zeroed in shared memory
+// first, so stale or uninitialised pool memory never reaches the output.
+// Stage layout: [panel][64 rows][128 B], 128-byte TMA swizzle (16-byte chunk c of row r
+// at c ^ (r & 7)).
+// ==================================================================================
+template <class T, int E, int STAGES>
+struct TmaCfg {
+    static constexpr int CW = 4;                       // consumer warps
+    static constexpr int NT = (CW + 1) * 32;
+    static constexpr int TILE = CW * 16;              // keys per window / stage
+    static constexpr int NPANEL = E / 64;             // 64-column (128-byte) panels
+    static constexpr int PANEL_BYTES = TILE * 128;
+    static constexpr int STAGE_BYTES = NPANEL * PANEL_BYTES;  // K (or V) bytes per stage
+    static constexpr int KS = E / 16;
+    static constexpr bool QREG = (E <= 128);
+    static constexpr size_t OFF_V = (size_t)STAGES * STAGE_BYTES;
+    static constexpr size_t OFF_Q = 2 * OFF_V;
+    static constexpr size_t OFF_O = OFF_Q + 16 * 2 * E;
+    static constexpr size_t OFF_ML = OFF_O + 16 * E * 4;
+    static constexpr size_t OFF_LSE = OFF_ML + CW * 16 * 2 * 4;
+    static constexpr size_t OFF_DESC = OFF_LSE + 16 * 4;
+    static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
+    static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
+    static constexpr size_t SMEM = OFF_FLAG + 16 + 1024;  // + alignment slack
+};
+
+struct StageDesc {
+    int ws, hkv, f, r0, n, flags;  // flags: 1 new_seg, 2 new_turn, 4 seg_last, 8 seg_complete, 16 first_piece
+};
+
+template <class T, int E, int STAGES>
+__global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(PagedParams p, const __grid_constant__ CUtensorMap tmk,
+                                                         const __grid_constant__ CUtensorMap tmv, int boxr) {
+    using C = TmaCfg<T, E, STAGES>;
+    constexpr int CW = C::CW, TILE = C::TILE, NPANEL = C::NPANEL;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t s0 = smem_u32(smem);
+    const uint32_t sK0 = s0, sV0 = s0 + (uint32_t)C::OFF_V, sQ0 = s0 + (uint32_t)C::OFF_Q;
+    uint8_t* sQ = smem + C::OFF_Q;
+    float* sO = reinterpret_cast<float*>(smem + C::OFF_O);
+    float* sML = reinterpret_cast<float*>(smem + C::OFF_ML);
+    float* sLse = reinterpret_cast<float*>(smem + C::OFF_LSE);
+    StageDesc* sDesc = reinterpret_cast<StageDesc*>(smem + C::OFF_DESC);
+    const uint32_t bar_full = s0 + (uint32_t)C::OFF_BAR;          // STAGES x 8 B
+    const uint32_t bar_empty = bar_full + STAGES * 8;            // STAGES x 8 B
+    volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
+
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const DecodeSched sch = *p.sched;
+    const int c = blockIdx.x;
+    if (c >= sch.n_eff) return;
+    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    if (u0 >= u1) return;
+    const int ws0 = find_row<C::NT>(p, u0);
+
+    if (tid == 0) {
+        for (int st = 0; st < STAGES; ++st) {
+            mbar_init(bar_full + st * 8, 1);
+            mbar_init(bar_empty + st * 8, CW);
+        }
+        *sAbort = 0;
+        fence_mbar_init();
+    }
+    for (int i = tid; i < 16 * E; i += C::NT) sO[i] = 0.f;
+    __syncthreads();
+
+    if (wid == CW) {
+        // =========================== producer warp ===========================
+        if (lane == 0) {
+            prefetch_tmap(&tmk);
+            prefetch_tmap(&tmv);
+        }
+        TileIter<TILE, true> it;
+        it.init(p, ws0, u0, u1);
+        const uint32_t box_bytes = (uint32_t)boxr * 128u;
+        int i = 0;
+        bool ok = true;
+        for (;; ++i) {
+            TileDesc d;
+            const bool have = it.next(p, d);
+            const int st = i % STAGES;
+            if (i >= STAGES && !*sAbort) {
+                if (!mbar_wait(bar_empty + st * 8, ((i / STAGES) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (!have) {
+                if (lane == 0) {
+                    sDesc[st].n = -1;
+                    mbar_arrive(bar_full + st * 8);
+                }
+                break;
+            }
+            const int win = d.pos0 & ~(TILE - 1);
+            int pfirst, npg;
+            if (p.BS <= TILE) {
+                pfirst = d.pos0 / p.BS;
+                npg = (d.pos0 + d.n - 1) / p.BS - pfirst + 1;
+            } else {
+                pfirst = win / p.BS;
+                npg = 1;
+            }
+            const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+            int page = lane < npg ? __ldg(btw + pfirst + lane) : 0;
+            if (lane == 0) {
+                StageDesc sd;
+                sd.ws = d.ws;
+                sd.hkv = d.hkv;
+                sd.f = d.f;
+                sd.r0 = d.pos0 - win;
+                sd.n = d.n;
+                sd.flags = (d.new_seg ? 1 : 0) | (d.new_turn ? 2 : 0) | (d.seg_last ? 4 : 0) |
+                           (d.seg_complete ? 8 : 0) | (d.first_piece ? 16 : 0);
+                sDesc[st] = sd;
+                mbar_expect_tx(bar_full + st * 8, (uint32_t)npg * NPANEL * 2u * box_bytes);
+            }
+            __syncwarp();
+            if (lane < npg) {
+                int z, srow;
+                const bool valid = p.NB <= 0 || (page >= 0 && page < p.NB);
+                if (p.BS <= TILE) {
+                    z = valid ? page * p.BS : -2 * boxr;
+                    srow = (pfirst + lane) * p.BS - win;
+                } else {
+                    z = valid ? page * p.BS + (win - pfirst * p.BS) : -2 * boxr;
+                    srow = 0;
+                }
+                const uint32_t kd = sK0 + st * C::STAGE_BYTES + srow * 128;
+                const uint32_t vd = sV0 + st * C::STAGE_BYTES + srow * 128;
+#pragma unroll
+                for (int pn = 0; pn < NPANEL; ++pn) {
+                    tma_load_3d(kd + pn * C::PANEL_BYTES, &tmk, pn * 64, d.hkv, z, bar_full + st * 8);
+                    tma_load_3d(vd + pn * C::PANEL_BYTES, &tmv, pn * 64, d.hkv, z, bar_full + st * 8);
+                }
+            }
+        }
+        if (!ok) {
+            if (lane == 0) {
+                *sAbort = 1;
+                atomicOr(&p.sched->error, 1);
+            }
+            // let the copies already issued land before the CTA can exit (bounded)
+            for (int j = (i - STAGES + 1 > 0 ? i - STAGES + 1 : 0); j < i; ++j)
+                mbar_wait(bar_full + (j % STAGES) * 8, (j / STAGES) & 1);
+        }
+        return;
+    }
+
+    // ============================ consumer warps ============================
+    uint32_t qf[C::QREG ? C::KS : 1][4];
+    float o[E / 8][4];
+    float m0 = 0.f, m1 = 0.f, l0 = 0.f, l1 = 0.f;
+    const float sl2 = p.scale_log2;
+    const int rb = wid * 16;
+    for (int i = 0;; ++i) {
+        if (named_bar_or(1, CW * 32, *sAbort != 0)) break;
+        const int st = i % STAGES;
+        if (!mbar_wait(bar_full + st * 8, (i / STAGES) & 1)) {
+            if (lane == 0) {
+                *sAbort = 1;
+                atomicOr(&p.sched->error, 2);
+            }
+            continue;
+        }
+        const StageDesc d = sDesc[st];
+        if (d.n < 0) break;
+        if (d.flags & 1) {
+            m0 = m1 = neg_inf();
+            l0 = l1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        }
+        if (d.flags & 2) {
+            named_bar_sync(2, CW * 32);
+            const int w = d.ws / p.S, s = d.ws - w * p.S;
+            const float* cr = p.cos + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
+            const float* sr = p.sin + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
+            for (int idx = tid; idx < 16 * (E / 8); idx += CW * 32) {
+                const int g = idx / (E / 8), ch = idx % (E / 8);
+                uint32_t pk[4] = {0u, 0u, 0u, 0u};
+                if (g < p.gqa) {
+                    const int hq = d.hkv * p.gqa + g;
+                    const T* qrow = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int e = ch * 8 + 2 * j;
+                        pk[j] = Elem<T>::pack2(rotated_elem(qrow, cr, sr, e, p.R),
+                                               rotated_elem(qrow, cr, sr, e + 1, p.R));
+                    }
+                }
+                *reinterpret_cast<uint4*>(sQ + (ch >> 3) * 2048 + g * 128 + (((ch & 7) ^ (g & 7)) << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+            named_bar_sync(2, CW * 32);
+            if constexpr (C::QREG) {
+#pragma unroll
+                for (int kk = 0; kk < C::KS; ++kk) {
+                    const int ch = kk * 2 + (lane >> 4), row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    ldsm_x4(sQ0 + (ch >> 3) * 2048 + row * 128 + (((ch & 7) ^ (row & 7)) << 4), qf[kk][0], qf[kk][1],
+                            qf[kk][2], qf[kk][3]);
+                }
+            }
+        }
+
+        const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
+        const uint32_t kb = sK0 + st * C::STAGE_BYTES, vb = sV0 + st * C::STAGE_BYTES;
+        if (hi > lo) {
+            const bool edge = (lo > 0) || (hi < 16);
+            if (edge) {
+                // zero the V rows of this warp's 16 keys that are outside the visible range
+                for (int idx = lane; idx < 16 * NPANEL * 8; idx += 32) {
+                    const int j = idx / (NPANEL * 8), rem = idx % (NPANEL * 8);
+                    if (j < lo || j >= hi)
+                        *reinterpret_cast<uint4*>(smem + C::OFF_V + (size_t)st * C::STAGE_BYTES + (rem >> 3) * C::PANEL_BYTES +
+                                                  (rb + j) * 128 + (rem & 7) * 16) = make_uint4(0u, 0u, 0u, 0u);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < C::KS; ++kk) {
+                uint32_t a[4];
+                if constexpr (C::QREG) {
+                    a[0] = qf[kk][0]; a[1] = qf[kk][1]; a[2] = qf[kk][2]; a[3] = qf[kk][3];
+                } else {
+                    const int ch = kk * 2 + (lane >> 4), row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    ldsm_x4(sQ0 + (ch >> 3) * 2048 + row * 128 + (((ch & 7) ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+                }
+                const int ch = kk * 2 + ((lane >> 3) & 1), row = rb + (lane & 7) + ((lane >> 4) << 3);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kb + (ch >> 3) * C::PANEL_BYTES + row * 128 + (((ch & 7) ^ (row & 7)) << 4), b0, b1, b2, b3);
+                Mma<T>::run(sc[0], a, b0, b1);
+                Mma<T>::run(sc[1], a, b2, b3);
+            }
+            float mx0 = neg_inf(), mx1 = neg_inf();
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col = nt * 8 + 2 * (lane & 3) + (j & 1);
+                    float x = sc[nt][j] * sl2;
+                    if (edge && (col < lo || col >= hi)) x = neg_inf();
+                    sc[nt][j] = x;
+                }
+                mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+                mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+            if (__any_sync(0xffffffffu, (n0 > m0) || (n1 > m1))) {
+                const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+                l0 *= al0;
+                l1 *= al1;
+#pragma unroll
+                for (int j = 0; j < E / 8; ++j) {
+                    o[j][0] *= al0; o[j][1] *= al0;
+                    o[j][2] *= al1; o[j][3] *= al1;
+                }
+                m0 = n0;
+                m1 = n1;
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sc[nt][0] = fast_exp2(sc[nt][0] - m0);
+                sc[nt][1] = fast_exp2(sc[nt][1] - m0);
+                sc[nt][2] = fast_exp2(sc[nt][2] - m1);
+                sc[nt][3] = fast_exp2(sc[nt][3] - m1);
+            }
+            l0 += (sc[0][0] + sc[0][1]) + (sc[1][0] + sc[1][1]);
+            l1 += (sc[0][2] + sc[0][3]) + (sc[1][2] + sc[1][3]);
+            uint32_t pa[4];
+            pa[0] = Elem<T>::pack2(sc[0][0], sc[0][1]);
+            pa[1] = Elem<T>::pack2(sc[0][2], sc[0][3]);
+            pa[2] = Elem<T>::pack2(sc[1][0], sc[1][1]);
+            pa[3] = Elem<T>::pack2(sc[1][2], sc[1][3]);
+#pragma unroll
+            for (int np = 0; np < E / 16; ++np) {
+                const int ch = 2 * np + (lane >> 4), row = rb + (lane & 7) + (((lane >> 3) & 1) << 3);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vb + (ch >> 3) * C::PANEL_BYTES + row * 128 + (((ch & 7) ^ (row & 7)) << 4), b0, b1, b2, b3);
+                Mma<T>::run(o[2 * np], pa, b0, b1);
+                Mma<T>::run(o[2 * np + 1], pa, b2, b3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_empty + st * 8);
+
+        if (d.flags & 4) {
+            // ---- combine the CW per-warp states of this segment piece ----
+            float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+            lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
+            float lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+            lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
+            const int r0 = lane >> 2;
+            if ((lane & 3) == 0) {
+                sML[(wid * 16 + r0) * 2 + 0] = m0;
+                sML[(wid * 16 + r0) * 2 + 1] = lt0;
+                sML[(wid * 16 + r0 + 8) * 2 + 0] = m1;
+                sML[(wid * 16 + r0 + 8) * 2 + 1] = lt1;
+            }
+            named_bar_sync(2, CW * 32);
+            float M0 = neg_inf(), M1 = neg_inf();
+#pragma unroll
+            for (int w2 = 0; w2 < CW; ++w2) {
+                M0 = fmaxf(M0, sML[(w2 * 16 + r0) * 2]);
+                M1 = fmaxf(M1, sML[(w2 * 16 + r0 + 8) * 2]);
+            }
+            float S0 = 0.f, S1 = 0.f;
+#pragma unroll
+            for (int w2 = 0; w2 < CW; ++w2) {
+                const float a0 = sML[(w2 * 16 + r0) * 2], a1 = sML[(w2 * 16 + r0 + 8) * 2];
+                if (a0 != neg_inf()) S0 += sML[(w2 * 16 + r0) * 2 + 1] * fast_exp2(a0 - M0);
+                if (a1 != neg_inf()) S1 += sML[(w2 * 16 + r0 + 8) * 2 + 1] * fast_exp2(a1 - M1);
+            }
+            const float f0 = (m0 != neg_inf() && S0 > 0.f) ? fast_exp2(m0 - M0) / S0 : 0.f;
+            const float f1 = (m1 != neg_inf() && S1 > 0.f) ? fast_exp2(m1 - M1) / S1 : 0.f;
+            if (wid == 0 && (lane & 3) == 0) {
+                sLse[r0] = S0 > 0.f ? M0 + __log2f(S0) : neg_inf();
+                sLse[r0 + 8] = S1 > 0.f ? M1 + __log2f(S1) : neg_inf();
+            }
+#pragma unroll 1
+            for (int w2 = 0; w2 < CW; ++w2) {
+                if (wid == w2) {
+#pragma unroll
+                    for (int j = 0; j < E / 8; ++j) {
+                        const int e = j * 8 + 2 * (lane & 3);
+                        float2* a = reinterpret_cast<float2*>(sO + r0 * E + e);
+                        float2* b = reinterpret_cast<float2*>(sO + (r0 + 8) * E + e);
+                        float2 va = *a, vb2 = *b;
+                        va.x += o[j][0] * f0; va.y += o[j][1] * f0;
+                        vb2.x += o[j][2] * f1; vb2.y += o[j][3] * f1;
+                        *a = va;
+                        *b = vb2;
+                    }
+                }
+                named_bar_sync(2, CW * 32);
+            }
+            const int w = d.ws / p.S, s = d.ws - w * p.S;
+            if (d.flags & 8) {
+                for (int idx = tid * 4; idx < 16 * E; idx += CW * 32 * 4) {
+                    const int g = idx / E, e = idx % E;
+                    float4 v = *reinterpret_cast<float4*>(sO + idx);
+                    *reinterpret_cast<float4*>(sO + idx) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (g < p.gqa) {
+                        const size_t orow = ((size_t)w * p.Hq + d.hkv * p.gqa + g) * p.S + s;
+                        T* op = static_cast<T*>(p.out) + orow * E + e;
+                        uint2 pk;
+                        pk.x = Elem<T>::pack2(v.x, v.y);
+                        pk.y = Elem<T>::pack2(v.z, v.w);
+                        *reinterpret_cast<uint2*>(op) = pk;
+                        if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) = v;
+                        if (p.lse_out && e == 0) p.lse_out[orow] = sLse[g] * kLn2;
+                    }
+                }
+            } else {
+                const int slot = 2 * c + ((d.flags & 16) ? 0 : 1);
+                for (int idx = tid * 4; idx < 16 * E; idx += CW * 32 * 4) {
+                    float4 v = *reinterpret_cast<float4*>(sO + idx);
+                    *reinterpret_cast<float4*>(sO + idx) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float4*>(p.part_o + (size_t)slot * 16 * E + idx) = v;
+                }
+                if (tid < 16) p.part_lse[slot * 16 + tid] = sLse[tid];
+            }
+            // sO / sML / sLse are reused only after the next segment's first named barrier
+        }
+    }
+}
+
+// ==================================================================================
 // f32 kernel (CUDA cores; tensor-core tf32 would miss the 1e-5 f32 tolerance)
 // thread t owns query head h = t / 8 for scores and the output columns
 // e = 4 * ((t % 8) + 8k) .. +3, so no cross-thread merge is needed.
@@ -585,7 +969,65 @@ struct KernelChoice {
     size_t smem;
     int nt;
     int min_units;
+    bool tma = false;
 };
+
+template <class T, int E>
+KernelChoice tma_choice() {
+    constexpr int STAGES = 3;
+    using C = TmaCfg<T, E, STAGES>;
+    return {reinterpret_cast<const void*>(&decode_tma_kernel<T, E, STAGES>), C::SMEM, C::NT, C::TILE, true};
+}
+
+// TMA path: 16-bit types, pages that tile the 64-key windows (BS | 64 with BS >= 8, or
+// 64 | BS), and pool token indices that fit the 32-bit TMA coordinate.
+bool tma_eligible(int dtype, int BS, long long NB) {
+    if (dtype != DVATTN_FLOAT16 && dtype != DVATTN_BFLOAT16) return false;
+    const bool small = BS >= 8 && BS <= 64 && (64 % BS) == 0;
+    const bool big = BS > 64 && (BS % 64) == 0;
+    return (small || big) && NB > 0 && NB * (long long)BS <= 0x7fffffffLL;
+}
+
+bool pick_tma(int dtype, int E, KernelChoice& kc) {
+    if (dtype == DVATTN_FLOAT16) {
+        if (E == 64) { kc = tma_choice<__half, 64>(); return true; }
+        if (E == 128) { kc = tma_choice<__half, 128>(); return true; }
+        if (E == 256) { kc = tma_choice<__half, 256>(); return true; }
+    } else if (dtype == DVATTN_BFLOAT16) {
+        if (E == 64) { kc = tma_choice<__nv_bfloat16, 64>(); return true; }
+        if (E == 128) { kc = tma_choice<__nv_bfloat16, 128>(); return true; }
+        if (E == 256) { kc = tma_choice<__nv_bfloat16, 256>(); return true; }
+    }
+    return false;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+// [tokens = NB*BS][Hkv][E] cache as a 3-D map, box = 64 columns x 1 head x boxr tokens,
+// 128-byte swizzle.
+bool encode_cache_map(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long tokens, int boxr) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)E, (cuuint64_t)Hkv, (cuuint64_t)tokens};
+    cuuint64_t strides[2] = {(cuuint64_t)E * 2, (cuuint64_t)Hkv * E * 2};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)boxr};
+    cuuint32_t es[3] = {1, 1, 1};
+    const CUtensorMapDataType dt =
+        dtype == DVATTN_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <class T, int E>
 KernelChoice tc_choice() {
@@ -668,10 +1110,15 @@ static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen) {
     return L;
 }
 
+static bool choose(int dtype, int E, int BS, long long NB, KernelChoice& kc) {
+    if (tma_eligible(dtype, BS, NB) && pick_tma(dtype, E, kc)) return true;
+    return pick_kernel(dtype, E, kc);
+}
+
 size_t decode_workspace_size(const dvattn_paged_args* a) {
     if (decode_validate(a) != DVATTN_OK) return 0;
     KernelChoice kc;
-    pick_kernel(a->dtype, a->E, kc);
+    choose(a->dtype, a->E, a->block_size, a->num_blocks, kc);
     int n_launch = 0;
     if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
     return decode_layout(a->W * a->S, a->E, n_launch, false).total;
@@ -681,7 +1128,7 @@ size_t decode_workspace_size(const dvattn_paged_args* a) {
 // cs_stride, cu_q/nseq); fills the workspace-derived fields.
 static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
     KernelChoice kc;
-    if (!pick_kernel(dtype, p.E, kc)) return DVATTN_ERR_UNSUPPORTED;
+    if (!choose(dtype, p.E, p.BS, p.NB, kc)) return DVATTN_ERR_UNSUPPORTED;
     int n_launch = 0;
     int st = device_sms_and_occ(kc, n_launch);
     if (st != DVATTN_OK) return st;
@@ -698,9 +1145,21 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
 
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) decode_prep_kernel<<<1, 1024, 0, stream>>>(p);
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_ATTEND) {
-        void* args[] = {&p};
-        if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)
-            return DVATTN_ERR_CUDA;
+        if (kc.tma) {
+            alignas(64) CUtensorMap mk, mv;
+            int boxr = p.BS < 64 ? p.BS : 64;
+            const long long tokens = p.NB * p.BS;
+            if (!encode_cache_map(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) ||
+                !encode_cache_map(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
+                return DVATTN_ERR_CUDA;
+            void* args[] = {&p, &mk, &mv, &boxr};
+            if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)
+                return DVATTN_ERR_CUDA;
+        } else {
+            void* args[] = {&p};
+            if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)
+                return DVATTN_ERR_CUDA;
+        }
     }
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_MERGE) {
         const unsigned segs = (unsigned)p.WS * (unsigned)p.Hkv;
@@ -761,7 +1220,7 @@ size_t varlen_workspace_size(const dvattn_varlen_args* v) {
     dvattn_paged_args a = varlen_as_paged(v);
     if (decode_validate(&a) != DVATTN_OK) return 0;
     KernelChoice kc;
-    pick_kernel(a.dtype, a.E, kc);
+    choose(a.dtype, a.E, a.block_size, a.num_blocks, kc);
     int n_launch = 0;
     if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
     return decode_layout(v->T, v->E, n_launch, true).total;

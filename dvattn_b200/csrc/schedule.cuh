@@ -24,7 +24,7 @@ namespace dvb {
 struct DecodeSched {
     long long U;  // total units
     int n_eff;    // CTAs that own units (<= n_launch)
-    int pad;
+    int error;    // nonzero: a bounded wait gave up (the outputs of this call are invalid)
 };
 
 // Device-side view of one paged decode call (passed by value).
@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
         long long want = (U + p.min_units - 1) / p.min_units;
         int n = (int)(want < p.n_launch ? want : p.n_launch);
         p.sched->U = U;
+        p.sched->error = 0;
         p.sched->n_eff = U > 0 ? (n > 0 ? n : 1) : 0;
     }
 }
@@ -155,7 +156,9 @@ struct TileDesc {
     bool new_seg, new_turn, seg_last, seg_complete, first_piece;
 };
 
-template <int TILE> struct TileIter {
+// ALIGN: tiles also never cross a TILE-aligned window of logical positions (so a tile's
+// rows map to fixed window rows, as the TMA kernel's page boxes need).
+template <int TILE, bool ALIGN = false> struct TileIter {
     int ws, hkv, f, t, off, vis;
     long long rem;
     int seg_left;
@@ -212,6 +215,10 @@ template <int TILE> struct TileIter {
         }
         int n = vis - t;
         if (n > TILE) n = TILE;
+        if (ALIGN) {
+            const int room = TILE - ((off + t) & (TILE - 1));
+            if (n > room) n = room;
+        }
         if ((long long)n > rem) n = (int)rem;
         d.ws = ws;
         d.hkv = hkv;
