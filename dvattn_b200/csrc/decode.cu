@@ -32,6 +32,95 @@ __device__ __forceinline__ float rotated_elem(const T* qrow, const float* cr, co
     return x;
 }
 
+
+// Rotated q of query row `ws`, turn `f`, for KV heads [h0, h0 + nh) into the swizzled
+// buffer sQ = [head][64-col panel][16 rows][128 B] (rows g >= gqa are zero).  Threads
+// tid < nth share the work; every global load of a thread is issued before any use, so
+// a rotation costs one memory latency.  Fast path when R/2 is a multiple of 8: a thread
+// owns a chunk of 8 rotary pairs (chunks c and c + R/16), or one pass-through chunk.
+template <class T, int E, int MAXT>
+__device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int f, int h0, int nh, uint8_t* sQ, int tid,
+                                              int nth) {
+    constexpr int CH = E / 8;
+    const int w = ws / p.S, s = ws - w * p.S;
+    const float* cr = p.cos + ((size_t)f * p.WS + ws) * p.cs_stride;
+    const float* sr = p.sin + ((size_t)f * p.WS + ws) * p.cs_stride;
+    const int R = p.R, hp = R >> 1;
+    auto dst = [&](int row, int ch) {
+        return reinterpret_cast<uint4*>(sQ + ((row >> 4) * (E / 64) + (ch >> 3)) * 2048 + (row & 15) * 128 +
+                                        (((ch & 7) ^ (row & 7)) << 4));
+    };
+    auto qrow_of = [&](int row) {
+        const int hq = (h0 + (row >> 4)) * p.gqa + (row & 15);
+        return static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+    };
+    if ((hp & 7) == 0 && ((reinterpret_cast<uintptr_t>(cr) | reinterpret_cast<uintptr_t>(sr)) & 15) == 0) {
+        const int npair = hp >> 3, npass = (E - R) >> 3;
+        const int per_row = npair + npass;
+        const int ntask = nh * 16 * per_row;
+        uint4 a[MAXT], b[MAXT];
+#pragma unroll
+        for (int k = 0; k < MAXT; ++k) {
+            const int t = tid + k * nth;
+            a[k] = b[k] = make_uint4(0u, 0u, 0u, 0u);
+            if (t < ntask) {
+                const int row = t / per_row, j = t - row * per_row;
+                if ((row & 15) < p.gqa) {
+                    const T* q = qrow_of(row);
+                    if (j < npair) {
+                        a[k] = *reinterpret_cast<const uint4*>(q + j * 8);
+                        b[k] = *reinterpret_cast<const uint4*>(q + j * 8 + hp);
+                    } else {
+                        a[k] = *reinterpret_cast<const uint4*>(q + R + (j - npair) * 8);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < MAXT; ++k) {
+            const int t = tid + k * nth;
+            if (t >= ntask) break;
+            const int row = t / per_row, j = t - row * per_row;
+            if (j < npair) {
+                const T* x = reinterpret_cast<const T*>(&a[k]);
+                const T* y = reinterpret_cast<const T*>(&b[k]);
+                const float4 c0 = *reinterpret_cast<const float4*>(cr + j * 8);
+                const float4 c1 = *reinterpret_cast<const float4*>(cr + j * 8 + 4);
+                const float4 s0 = *reinterpret_cast<const float4*>(sr + j * 8);
+                const float4 s1 = *reinterpret_cast<const float4*>(sr + j * 8 + 4);
+                const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                uint32_t lo[4], hi[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float x0 = Elem<T>::to_f(x[2 * u]), x1 = Elem<T>::to_f(x[2 * u + 1]);
+                    const float y0 = Elem<T>::to_f(y[2 * u]), y1 = Elem<T>::to_f(y[2 * u + 1]);
+                    lo[u] = Elem<T>::pack2(x0 * cc[2 * u] - y0 * ss[2 * u], x1 * cc[2 * u + 1] - y1 * ss[2 * u + 1]);
+                    hi[u] = Elem<T>::pack2(y0 * cc[2 * u] + x0 * ss[2 * u], y1 * cc[2 * u + 1] + x1 * ss[2 * u + 1]);
+                }
+                *dst(row, j) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *dst(row, j + (hp >> 3)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            } else {
+                *dst(row, (R >> 3) + (j - npair)) = a[k];
+            }
+        }
+    } else {
+        for (int t = tid; t < nh * 16 * CH; t += nth) {
+            const int row = t / CH, ch = t - row * CH;
+            uint32_t pk[4] = {0u, 0u, 0u, 0u};
+            if ((row & 15) < p.gqa) {
+                const T* q = qrow_of(row);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int e = ch * 8 + 2 * u;
+                    pk[u] = Elem<T>::pack2(rotated_elem(q, cr, sr, e, R), rotated_elem(q, cr, sr, e + 1, R));
+                }
+            }
+            *dst(row, ch) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+    }
+}
+
 // ==================================================================================
 // tensor-core kernel (f16 / bf16)
 // ==================================================================================
@@ -344,7 +433,7 @@ struct TmaCfg {
     static constexpr size_t OFF_DESC = OFF_LSE + 16 * 4;
     static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
     static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
-    static constexpr size_t SMEM = OFF_FLAG + 16 + 1024;  // + alignment slack
+    static constexpr size_t SMEM = OFF_FLAG + 16;
 };
 
 struct StageDesc {
@@ -356,9 +445,12 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
                                                          const __grid_constant__ CUtensorMap tmv, int boxr) {
     using C = TmaCfg<T, E, STAGES>;
     constexpr int CW = C::CW, TILE = C::TILE, NPANEL = C::NPANEL;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t s0 = smem_u32(smem);
+    if (s0 & 1023) {
+        if (threadIdx.x == 0) atomicOr(&p.sched->error, 4);
+        return;
+    }
     const uint32_t sK0 = s0, sV0 = s0 + (uint32_t)C::OFF_V, sQ0 = s0 + (uint32_t)C::OFF_Q;
     uint8_t* sQ = smem + C::OFF_Q;
     float* sO = reinterpret_cast<float*>(smem + C::OFF_O);
@@ -394,8 +486,9 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
         }
-        TileIter<TILE, true> it;
+        TileIter<TILE> it;
         it.init(p, ws0, u0, u1);
+        it.align = TILE;
         const uint32_t box_bytes = (uint32_t)boxr * 128u;
         int i = 0;
         bool ok = true;
@@ -497,25 +590,7 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
         }
         if (d.flags & 2) {
             named_bar_sync(2, CW * 32);
-            const int w = d.ws / p.S, s = d.ws - w * p.S;
-            const float* cr = p.cos + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
-            const float* sr = p.sin + ((size_t)d.f * p.WS + d.ws) * p.cs_stride;
-            for (int idx = tid; idx < 16 * (E / 8); idx += CW * 32) {
-                const int g = idx / (E / 8), ch = idx % (E / 8);
-                uint32_t pk[4] = {0u, 0u, 0u, 0u};
-                if (g < p.gqa) {
-                    const int hq = d.hkv * p.gqa + g;
-                    const T* qrow = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int e = ch * 8 + 2 * j;
-                        pk[j] = Elem<T>::pack2(rotated_elem(qrow, cr, sr, e, p.R),
-                                               rotated_elem(qrow, cr, sr, e + 1, p.R));
-                    }
-                }
-                *reinterpret_cast<uint4*>(sQ + (ch >> 3) * 2048 + g * 128 + (((ch & 7) ^ (g & 7)) << 4)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
+            rotate_q_rows<T, E, (16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, d.hkv, 1, sQ, tid, CW * 32);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -691,6 +766,417 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
                 if (tid < 16) p.part_lse[slot * 16 + tid] = sLse[tid];
             }
             // sO / sML / sLse are reused only after the next segment's first named barrier
+        }
+    }
+}
+
+// ==================================================================================
+// Row kernel (f16 / bf16, Hkv | CW): like the TMA kernel, but a CTA streams ALL KV heads
+// of its keys.  A stage holds TOKB = 16*CW/Hkv keys x Hkv heads; consumer warp w serves
+// head w % Hkv and keys [16*(w / Hkv), +16) of the stage.  The producer issues the boxes
+// of every head of a page back to back, so the page's K (and V) rows -- Hkv*E elements
+// contiguous per token -- are fetched from DRAM together instead of head by head at
+// unrelated times.  Stage layout: slab (head h, panel p) = TOKB rows x 128 B, swizzled.
+// ==================================================================================
+template <class T, int E, int CW, int STAGES>
+struct RowCfg {
+    static constexpr int NT = (CW + 1) * 32;
+    static constexpr int NPANEL = E / 64;
+    static constexpr int KROWS = CW * 16;                         // key-head rows per stage
+    static constexpr int STAGE_BYTES = KROWS * NPANEL * 128;      // K (or V) bytes per stage
+    static constexpr int KS = E / 16;
+    static constexpr bool QREG = (E <= 128);
+    static constexpr int QBYTES = CW * 16 * 2 * E;                // rotated q of up to CW heads x 16 rows
+    static constexpr int OBYTES = 2 * 16 * E * 4;                 // merge buffer (Hkv <= 2 only)
+    static constexpr size_t OFF_V = (size_t)STAGES * STAGE_BYTES;
+    static constexpr size_t OFF_Q = 2 * OFF_V;
+    // With q fragments held in registers (E <= 128) the rotation buffer is only used at a
+    // turn change and the merge buffer only at a row's end, so the two share memory.
+    static constexpr size_t OFF_O = QREG ? OFF_Q : OFF_Q + QBYTES;
+    static constexpr size_t OFF_ML = QREG ? OFF_Q + (QBYTES > OBYTES ? QBYTES : OBYTES) : OFF_O + OBYTES;
+    static constexpr size_t OFF_LSE = OFF_ML + CW * 16 * 2 * 4;
+    static constexpr size_t OFF_DESC = OFF_LSE + 2 * 16 * 4;
+    static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
+    static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
+    static constexpr size_t SMEM = OFF_FLAG + 16;
+};
+
+template <class T, int E, int CW, int STAGES>
+__global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
+    decode_row_kernel(PagedParams p, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                      int boxr) {
+    using C = RowCfg<T, E, CW, STAGES>;
+    constexpr int NPANEL = C::NPANEL;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const uint32_t s0 = smem_u32(smem);
+    if (s0 & 1023) {  // the 128-byte TMA swizzle pattern needs 1024-byte aligned stages
+        if (threadIdx.x == 0) atomicOr(&p.sched->error, 4);
+        return;
+    }
+    const uint32_t sK0 = s0, sV0 = s0 + (uint32_t)C::OFF_V, sQ0 = s0 + (uint32_t)C::OFF_Q;
+    uint8_t* sQ = smem + C::OFF_Q;
+    float* sO = reinterpret_cast<float*>(smem + C::OFF_O);
+    float* sML = reinterpret_cast<float*>(smem + C::OFF_ML);
+    float* sLse = reinterpret_cast<float*>(smem + C::OFF_LSE);
+    StageDesc* sDesc = reinterpret_cast<StageDesc*>(smem + C::OFF_DESC);
+    const uint32_t bar_full = s0 + (uint32_t)C::OFF_BAR;
+    const uint32_t bar_empty = bar_full + STAGES * 8;
+    volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
+
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int Hkv = p.Hkv;
+    const int TOKB = (CW / Hkv) * 16;           // keys per stage (window)
+    const int SLAB = TOKB * 128;                // bytes of one (head, panel) slab
+    const DecodeSched sch = *p.sched;
+    const int c = blockIdx.x;
+    if (c >= sch.n_eff) return;
+    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    if (u0 >= u1) return;
+    const int ws0 = find_row<C::NT>(p, u0);
+
+    if (tid == 0) {
+        for (int st = 0; st < STAGES; ++st) {
+            mbar_init(bar_full + st * 8, 1);
+            mbar_init(bar_empty + st * 8, CW);
+        }
+        *sAbort = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (wid == CW) {
+        // =========================== producer warp ===========================
+        if (lane == 0) {
+            prefetch_tmap(&tmk);
+            prefetch_tmap(&tmv);
+        }
+        TileIter<64> it;
+        it.init(p, ws0, u0, u1);
+        it.align = TOKB;
+        const uint32_t box_bytes = (uint32_t)boxr * 128u;
+        int i = 0;
+        bool ok = true;
+        for (;; ++i) {
+            TileDesc d;
+            const bool have = it.next(p, d);
+            const int st = i % STAGES;
+            if (i >= STAGES && !*sAbort) {
+                if (!mbar_wait(bar_empty + st * 8, ((i / STAGES) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (!have) {
+                if (lane == 0) {
+                    sDesc[st].n = -1;
+                    mbar_arrive(bar_full + st * 8);
+                }
+                break;
+            }
+            const int win = d.pos0 & ~(TOKB - 1);
+            int pfirst, npg;
+            if (p.BS <= TOKB) {
+                pfirst = d.pos0 / p.BS;
+                npg = (d.pos0 + d.n - 1) / p.BS - pfirst + 1;
+            } else {
+                pfirst = win / p.BS;
+                npg = 1;
+            }
+            const int ntask = npg * Hkv;  // (page, head) pairs, <= 32
+            const int pg = lane / Hkv, hh = lane - pg * Hkv;
+            const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+            const int page = lane < ntask ? __ldg(btw + pfirst + pg) : 0;
+            if (lane == 0) {
+                StageDesc sd;
+                sd.ws = d.ws;
+                sd.hkv = 0;
+                sd.f = d.f;
+                sd.r0 = d.pos0 - win;
+                sd.n = d.n;
+                sd.flags = (d.new_seg ? 1 : 0) | (d.new_turn ? 2 : 0) | (d.seg_last ? 4 : 0) |
+                           (d.seg_complete ? 8 : 0) | (d.first_piece ? 16 : 0);
+                sDesc[st] = sd;
+                mbar_expect_tx(bar_full + st * 8, (uint32_t)ntask * NPANEL * 2u * box_bytes);
+            }
+            __syncwarp();
+            if (lane < ntask) {
+                int z, srow;
+                const bool valid = p.NB <= 0 || (page >= 0 && page < p.NB);
+                if (p.BS <= TOKB) {
+                    z = valid ? page * p.BS : -2 * boxr;
+                    srow = (pfirst + pg) * p.BS - win;
+                } else {
+                    z = valid ? page * p.BS + (win - pfirst * p.BS) : -2 * boxr;
+                    srow = 0;
+                }
+                const uint32_t off = (uint32_t)(st * C::STAGE_BYTES + hh * NPANEL * SLAB + srow * 128);
+#pragma unroll
+                for (int pn = 0; pn < NPANEL; ++pn) {
+                    tma_load_3d(sK0 + off + pn * SLAB, &tmk, pn * 64, hh, z, bar_full + st * 8);
+                    tma_load_3d(sV0 + off + pn * SLAB, &tmv, pn * 64, hh, z, bar_full + st * 8);
+                }
+            }
+        }
+        if (!ok) {
+            if (lane == 0) {
+                *sAbort = 1;
+                atomicOr(&p.sched->error, 1);
+            }
+            for (int j = (i - STAGES + 1 > 0 ? i - STAGES + 1 : 0); j < i; ++j)
+                mbar_wait(bar_full + (j % STAGES) * 8, (j / STAGES) & 1);
+        }
+        return;
+    }
+
+    // ============================ consumer warps ============================
+    const int h = wid % Hkv, grp = wid / Hkv;
+    const int rb = grp * 16;                    // this warp's first key row in the window
+    const int wph = CW / Hkv;                   // warps per head
+    uint32_t qf[C::QREG ? C::KS : 1][4];
+    float o[E / 8][4];
+    float m0 = 0.f, m1 = 0.f, l0 = 0.f, l1 = 0.f;
+    const float sl2 = p.scale_log2;
+    const uint32_t qh = sQ0 + h * NPANEL * 2048;
+    for (int i = 0;; ++i) {
+        if (named_bar_or(1, CW * 32, *sAbort != 0)) break;
+        const int st = i % STAGES;
+        if (!mbar_wait(bar_full + st * 8, (i / STAGES) & 1)) {
+            if (lane == 0) {
+                *sAbort = 1;
+                atomicOr(&p.sched->error, 2);
+            }
+            continue;
+        }
+        const StageDesc d = sDesc[st];
+        if (d.n < 0) break;
+        if (d.flags & 1) {
+            m0 = m1 = neg_inf();
+            l0 = l1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        }
+        if (d.flags & 2) {
+            named_bar_sync(2, CW * 32);
+            rotate_q_rows<T, E, (CW * 16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, 0, Hkv, sQ, tid, CW * 32);
+            named_bar_sync(2, CW * 32);
+            if constexpr (C::QREG) {
+#pragma unroll
+                for (int kk = 0; kk < C::KS; ++kk) {
+                    const int ch = kk * 2 + (lane >> 4), row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    ldsm_x4(qh + (ch >> 3) * 2048 + row * 128 + (((ch & 7) ^ (row & 7)) << 4), qf[kk][0], qf[kk][1],
+                            qf[kk][2], qf[kk][3]);
+                }
+            }
+        }
+
+        const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
+        const uint32_t kb = sK0 + st * C::STAGE_BYTES + h * NPANEL * SLAB;
+        const uint32_t vb = sV0 + st * C::STAGE_BYTES + h * NPANEL * SLAB;
+        if (hi > lo) {
+            const bool edge = (lo > 0) || (hi < 16);
+            if (edge) {
+                uint8_t* vrow = smem + C::OFF_V + (size_t)st * C::STAGE_BYTES + (size_t)h * NPANEL * SLAB;
+                for (int idx = lane; idx < 16 * NPANEL * 8; idx += 32) {
+                    const int j = idx / (NPANEL * 8), rem = idx % (NPANEL * 8);
+                    if (j < lo || j >= hi)
+                        *reinterpret_cast<uint4*>(vrow + (rem >> 3) * SLAB + (rb + j) * 128 + (rem & 7) * 16) =
+                            make_uint4(0u, 0u, 0u, 0u);
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+            }
+            float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+            for (int kk = 0; kk < C::KS; ++kk) {
+                uint32_t a[4];
+                if constexpr (C::QREG) {
+                    a[0] = qf[kk][0]; a[1] = qf[kk][1]; a[2] = qf[kk][2]; a[3] = qf[kk][3];
+                } else {
+                    const int ch = kk * 2 + (lane >> 4), row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    ldsm_x4(qh + (ch >> 3) * 2048 + row * 128 + (((ch & 7) ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+                }
+                const int ch = kk * 2 + ((lane >> 3) & 1), row = rb + (lane & 7) + ((lane >> 4) << 3);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kb + (ch >> 3) * SLAB + row * 128 + (((ch & 7) ^ (row & 7)) << 4), b0, b1, b2, b3);
+                Mma<T>::run(sc[0], a, b0, b1);
+                Mma<T>::run(sc[1], a, b2, b3);
+            }
+            float mx0 = neg_inf(), mx1 = neg_inf();
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int col = nt * 8 + 2 * (lane & 3) + (j & 1);
+                    float x = sc[nt][j] * sl2;
+                    if (edge && (col < lo || col >= hi)) x = neg_inf();
+                    sc[nt][j] = x;
+                }
+                mx0 = fmaxf(mx0, fmaxf(sc[nt][0], sc[nt][1]));
+                mx1 = fmaxf(mx1, fmaxf(sc[nt][2], sc[nt][3]));
+            }
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+            const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
+            if (__any_sync(0xffffffffu, (n0 > m0) || (n1 > m1))) {
+                const float al0 = fast_exp2(m0 - n0), al1 = fast_exp2(m1 - n1);
+                l0 *= al0;
+                l1 *= al1;
+#pragma unroll
+                for (int j = 0; j < E / 8; ++j) {
+                    o[j][0] *= al0; o[j][1] *= al0;
+                    o[j][2] *= al1; o[j][3] *= al1;
+                }
+                m0 = n0;
+                m1 = n1;
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                sc[nt][0] = fast_exp2(sc[nt][0] - m0);
+                sc[nt][1] = fast_exp2(sc[nt][1] - m0);
+                sc[nt][2] = fast_exp2(sc[nt][2] - m1);
+                sc[nt][3] = fast_exp2(sc[nt][3] - m1);
+            }
+            l0 += (sc[0][0] + sc[0][1]) + (sc[1][0] + sc[1][1]);
+            l1 += (sc[0][2] + sc[0][3]) + (sc[1][2] + sc[1][3]);
+            uint32_t pa[4];
+            pa[0] = Elem<T>::pack2(sc[0][0], sc[0][1]);
+            pa[1] = Elem<T>::pack2(sc[0][2], sc[0][3]);
+            pa[2] = Elem<T>::pack2(sc[1][0], sc[1][1]);
+            pa[3] = Elem<T>::pack2(sc[1][2], sc[1][3]);
+#pragma unroll
+            for (int np = 0; np < E / 16; ++np) {
+                const int ch = 2 * np + (lane >> 4), row = rb + (lane & 7) + (((lane >> 3) & 1) << 3);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vb + (ch >> 3) * SLAB + row * 128 + (((ch & 7) ^ (row & 7)) << 4), b0, b1, b2, b3);
+                Mma<T>::run(o[2 * np], pa, b0, b1);
+                Mma<T>::run(o[2 * np + 1], pa, b2, b3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_empty + st * 8);
+
+        if (d.flags & 4) {
+            // ---- finish this row piece: per head, combine its wph warps ----
+            float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+            lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
+            float lt1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+            lt1 += __shfl_xor_sync(0xffffffffu, lt1, 2);
+            const int r0 = lane >> 2;
+            float M0 = m0, M1 = m1, S0 = lt0, S1 = lt1;
+            float f0, f1;
+            if (wph > 1) {
+                if ((lane & 3) == 0) {
+                    sML[(wid * 16 + r0) * 2 + 0] = m0;
+                    sML[(wid * 16 + r0) * 2 + 1] = lt0;
+                    sML[(wid * 16 + r0 + 8) * 2 + 0] = m1;
+                    sML[(wid * 16 + r0 + 8) * 2 + 1] = lt1;
+                }
+                named_bar_sync(2, CW * 32);
+                M0 = M1 = neg_inf();
+                for (int g2 = 0; g2 < wph; ++g2) {
+                    const int w2 = g2 * Hkv + h;
+                    M0 = fmaxf(M0, sML[(w2 * 16 + r0) * 2]);
+                    M1 = fmaxf(M1, sML[(w2 * 16 + r0 + 8) * 2]);
+                }
+                S0 = S1 = 0.f;
+                for (int g2 = 0; g2 < wph; ++g2) {
+                    const int w2 = g2 * Hkv + h;
+                    const float a0 = sML[(w2 * 16 + r0) * 2], a1 = sML[(w2 * 16 + r0 + 8) * 2];
+                    if (a0 != neg_inf()) S0 += sML[(w2 * 16 + r0) * 2 + 1] * fast_exp2(a0 - M0);
+                    if (a1 != neg_inf()) S1 += sML[(w2 * 16 + r0 + 8) * 2 + 1] * fast_exp2(a1 - M1);
+                }
+            }
+            f0 = (m0 != neg_inf() && S0 > 0.f) ? fast_exp2(m0 - M0) / S0 : 0.f;
+            f1 = (m1 != neg_inf() && S1 > 0.f) ? fast_exp2(m1 - M1) / S1 : 0.f;
+            const float lse0 = S0 > 0.f ? M0 + __log2f(S0) : neg_inf();
+            const float lse1 = S1 > 0.f ? M1 + __log2f(S1) : neg_inf();
+            const int w = d.ws / p.S, s = d.ws - w * p.S;
+            const bool complete = (d.flags & 8) != 0;
+            const int slot = 2 * c + ((d.flags & 16) ? 0 : 1);
+            if (wph == 1) {
+                // this warp alone holds head h: write straight from the fragments
+                const int ga = r0, gb = r0 + 8;
+                if (complete) {
+                    const size_t oa = ((size_t)w * p.Hq + h * p.gqa + ga) * p.S + s;
+                    const size_t ob = ((size_t)w * p.Hq + h * p.gqa + gb) * p.S + s;
+                    T* pa_ = static_cast<T*>(p.out) + oa * E;
+                    T* pb_ = static_cast<T*>(p.out) + ob * E;
+#pragma unroll
+                    for (int j = 0; j < E / 8; ++j) {
+                        const int e = j * 8 + 2 * (lane & 3);
+                        if (ga < p.gqa) {
+                            *reinterpret_cast<uint32_t*>(pa_ + e) = Elem<T>::pack2(o[j][0] * f0, o[j][1] * f0);
+                            if (p.out_f32) *reinterpret_cast<float2*>(p.out_f32 + oa * E + e) = make_float2(o[j][0] * f0, o[j][1] * f0);
+                        }
+                        if (gb < p.gqa) {
+                            *reinterpret_cast<uint32_t*>(pb_ + e) = Elem<T>::pack2(o[j][2] * f1, o[j][3] * f1);
+                            if (p.out_f32) *reinterpret_cast<float2*>(p.out_f32 + ob * E + e) = make_float2(o[j][2] * f1, o[j][3] * f1);
+                        }
+                    }
+                    if (p.lse_out && (lane & 3) == 0) {
+                        if (ga < p.gqa) p.lse_out[oa] = lse0 * kLn2;
+                        if (gb < p.gqa) p.lse_out[ob] = lse1 * kLn2;
+                    }
+                } else {
+                    float* po = p.part_o + ((size_t)(slot * Hkv + h) * 16) * E;
+#pragma unroll
+                    for (int j = 0; j < E / 8; ++j) {
+                        const int e = j * 8 + 2 * (lane & 3);
+                        *reinterpret_cast<float2*>(po + r0 * E + e) = make_float2(o[j][0] * f0, o[j][1] * f0);
+                        *reinterpret_cast<float2*>(po + (r0 + 8) * E + e) = make_float2(o[j][2] * f1, o[j][3] * f1);
+                    }
+                    if ((lane & 3) == 0) {
+                        p.part_lse[(slot * Hkv + h) * 16 + r0] = lse0;
+                        p.part_lse[(slot * Hkv + h) * 16 + r0 + 8] = lse1;
+                    }
+                }
+            } else {
+                // wph warps per head (Hkv <= 2): fixed-order sum in sO[h], then write
+                float* so = sO + h * 16 * E;
+                if (grp == 0 && (lane & 3) == 0) {
+                    sLse[h * 16 + r0] = lse0;
+                    sLse[h * 16 + r0 + 8] = lse1;
+                }
+#pragma unroll 1
+                for (int g2 = 0; g2 < wph; ++g2) {
+                    if (grp == g2) {
+#pragma unroll
+                        for (int j = 0; j < E / 8; ++j) {
+                            const int e = j * 8 + 2 * (lane & 3);
+                            float2* a = reinterpret_cast<float2*>(so + r0 * E + e);
+                            float2* b = reinterpret_cast<float2*>(so + (r0 + 8) * E + e);
+                            float2 va = g2 ? *a : make_float2(0.f, 0.f), vb2 = g2 ? *b : make_float2(0.f, 0.f);
+                            va.x += o[j][0] * f0; va.y += o[j][1] * f0;
+                            vb2.x += o[j][2] * f1; vb2.y += o[j][3] * f1;
+                            *a = va;
+                            *b = vb2;
+                        }
+                    }
+                    named_bar_sync(2, CW * 32);
+                }
+                for (int idx = tid * 4; idx < Hkv * 16 * E; idx += CW * 32 * 4) {
+                    const int hg = idx / E, e = idx % E;
+                    const int hk = hg >> 4, g = hg & 15;
+                    const float4 v = *reinterpret_cast<float4*>(sO + idx);
+                    if (complete) {
+                        if (g < p.gqa) {
+                            const size_t orow = ((size_t)w * p.Hq + hk * p.gqa + g) * p.S + s;
+                            T* op = static_cast<T*>(p.out) + orow * E + e;
+                            uint2 pk;
+                            pk.x = Elem<T>::pack2(v.x, v.y);
+                            pk.y = Elem<T>::pack2(v.z, v.w);
+                            *reinterpret_cast<uint2*>(op) = pk;
+                            if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) = v;
+                            if (p.lse_out && e == 0) p.lse_out[orow] = sLse[hg] * kLn2;
+                        }
+                    } else {
+                        *reinterpret_cast<float4*>(p.part_o + ((size_t)slot * Hkv * 16) * E + idx) = v;
+                        if (e == 0) p.part_lse[slot * Hkv * 16 + hg] = sLse[hg];
+                    }
+                }
+            }
         }
     }
 }
@@ -917,27 +1403,29 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E)
         }
         return;
     }
-    const long long b = P0 * p.Hkv + hkv * V;
+    const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
     const int n = sch.n_eff;
     const int ca = cta_of(b, sch.U, n), cb = cta_of(b + V - 1, sch.U, n);
     if (ca == cb || r >= p.gqa) return;
+    const int hh = p.slot_heads > 1 ? hkv : 0;
+    auto part = [&](int c) {
+        const int slot = (c == ca && cta_start(ca, sch.U, n) < b) ? 2 * ca + 1 : 2 * c;
+        return (slot * p.slot_heads + hh) * 16 + r;
+    };
 
     float lmax = neg_inf();
-    for (int c = ca; c <= cb; ++c) {
-        const int slot = (c == ca && cta_start(ca, sch.U, n) < b) ? 2 * ca + 1 : 2 * c;
-        lmax = fmaxf(lmax, p.part_lse[slot * 16 + r]);
-    }
+    for (int c = ca; c <= cb; ++c) lmax = fmaxf(lmax, p.part_lse[part(c)]);
     float acc[32];
     const int nchunk = E / 32;  // float4 chunks per thread
     for (int j = 0; j < 4 * nchunk; ++j) acc[j] = 0.f;
     float den = 0.f;
     for (int c = ca; c <= cb; ++c) {
-        const int slot = (c == ca && cta_start(ca, sch.U, n) < b) ? 2 * ca + 1 : 2 * c;
-        const float ls = p.part_lse[slot * 16 + r];
+        const int pi = part(c);
+        const float ls = p.part_lse[pi];
         if (ls == neg_inf()) continue;
         const float wgt = fast_exp2(ls - lmax);
         den += wgt;
-        const float* po = p.part_o + ((size_t)slot * 16 + r) * E;
+        const float* po = p.part_o + (size_t)pi * E;
         for (int j = 0; j < nchunk; ++j) {
             const float4 v = *reinterpret_cast<const float4*>(po + 4 * (sub + 8 * j));
             acc[4 * j + 0] += wgt * v.x;
@@ -970,7 +1458,43 @@ struct KernelChoice {
     int nt;
     int min_units;
     bool tma = false;
+    bool row = false;  // all KV heads per CTA (hsplit = 1)
+    int cw = 4;
 };
+
+template <class T, int E, int CW, int STAGES>
+KernelChoice row_choice() {
+    using C = RowCfg<T, E, CW, STAGES>;
+    KernelChoice k{reinterpret_cast<const void*>(&decode_row_kernel<T, E, CW, STAGES>), C::SMEM, C::NT, 64, true};
+    k.row = true;
+    k.cw = CW;
+    return k;
+}
+
+// Row kernel: 16-bit types, Hkv in {1, 2, 4} (4 consumer warps) or 8 (8 warps), pages
+// that tile the TOKB = 16*CW/Hkv-key windows.
+bool pick_row(int dtype, int E, int Hkv, int BS, long long NB, KernelChoice& kc) {
+    if (dtype != DVATTN_FLOAT16 && dtype != DVATTN_BFLOAT16) return false;
+    if (!(Hkv == 1 || Hkv == 2 || Hkv == 4 || Hkv == 8)) return false;
+    if (Hkv == 8 && E != 128 && E != 64) return false;
+    const int cw = Hkv == 8 ? 8 : 4;
+    const int tokb = 16 * cw / Hkv;
+    const bool small = BS >= 8 && BS <= tokb && (tokb % BS) == 0;
+    const bool big = BS > tokb && (BS % tokb) == 0;
+    if (!(small || big) || NB <= 0 || NB * (long long)BS > 0x7fffffffLL) return false;
+#define DVB_ROW(TT)                                                              \
+    if (cw == 8) {                                                               \
+        if (E == 64) { kc = row_choice<TT, 64, 8, 3>(); return true; }           \
+        if (E == 128) { kc = row_choice<TT, 128, 8, 3>(); return true; }         \
+    } else {                                                                     \
+        if (E == 64) { kc = row_choice<TT, 64, 4, 3>(); return true; }           \
+        if (E == 128) { kc = row_choice<TT, 128, 4, 3>(); return true; }         \
+        if (E == 256) { kc = row_choice<TT, 256, 4, 2>(); return true; }         \
+    }
+    if (dtype == DVATTN_FLOAT16) { DVB_ROW(__half) } else { DVB_ROW(__nv_bfloat16) }
+#undef DVB_ROW
+    return false;
+}
 
 template <class T, int E>
 KernelChoice tma_choice() {
@@ -1099,18 +1623,19 @@ static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
 struct DecodeLayout {
     size_t off_P, off_rs, off_po, off_pl, total;
 };
-static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen) {
+static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int slot_heads) {
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
     DecodeLayout L;
     L.off_P = 256;
     L.off_rs = L.off_P + up(sizeof(long long) * (size_t)(WS + 1));
     L.off_po = L.off_rs + (varlen ? up(sizeof(int) * (size_t)WS) : 0);
-    L.off_pl = L.off_po + up(sizeof(float) * (size_t)n_launch * 2 * 16 * E);
-    L.total = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * 16);
+    L.off_pl = L.off_po + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16 * E);
+    L.total = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16);
     return L;
 }
 
-static bool choose(int dtype, int E, int BS, long long NB, KernelChoice& kc) {
+static bool choose(int dtype, int E, int Hkv, int BS, long long NB, KernelChoice& kc) {
+    if (pick_row(dtype, E, Hkv, BS, NB, kc)) return true;
     if (tma_eligible(dtype, BS, NB) && pick_tma(dtype, E, kc)) return true;
     return pick_kernel(dtype, E, kc);
 }
@@ -1118,21 +1643,23 @@ static bool choose(int dtype, int E, int BS, long long NB, KernelChoice& kc) {
 size_t decode_workspace_size(const dvattn_paged_args* a) {
     if (decode_validate(a) != DVATTN_OK) return 0;
     KernelChoice kc;
-    choose(a->dtype, a->E, a->block_size, a->num_blocks, kc);
+    choose(a->dtype, a->E, a->Hkv, a->block_size, a->num_blocks, kc);
     int n_launch = 0;
     if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
-    return decode_layout(a->W * a->S, a->E, n_launch, false).total;
+    return decode_layout(a->W * a->S, a->E, n_launch, false, kc.row ? a->Hkv : 1).total;
 }
 
 // Runs prep -> split kernel -> merge for a filled PagedParams (pointers, sizes, R,
 // cs_stride, cu_q/nseq); fills the workspace-derived fields.
 static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
     KernelChoice kc;
-    if (!choose(dtype, p.E, p.BS, p.NB, kc)) return DVATTN_ERR_UNSUPPORTED;
+    if (!choose(dtype, p.E, p.Hkv, p.BS, p.NB, kc)) return DVATTN_ERR_UNSUPPORTED;
     int n_launch = 0;
     int st = device_sms_and_occ(kc, n_launch);
     if (st != DVATTN_OK) return st;
-    const DecodeLayout L = decode_layout(p.WS, p.E, n_launch, p.cu_q != nullptr);
+    p.hsplit = kc.row ? 1 : p.Hkv;
+    p.slot_heads = kc.row ? p.Hkv : 1;
+    const DecodeLayout L = decode_layout(p.WS, p.E, n_launch, p.cu_q != nullptr, p.slot_heads);
     if (!workspace || wbytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255)) return DVATTN_ERR_WORKSPACE;
     char* wsb = static_cast<char*>(workspace);
     p.sched = reinterpret_cast<DecodeSched*>(wsb);
@@ -1147,7 +1674,8 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_ATTEND) {
         if (kc.tma) {
             alignas(64) CUtensorMap mk, mv;
-            int boxr = p.BS < 64 ? p.BS : 64;
+            const int win = kc.row ? 16 * kc.cw / p.Hkv : 64;
+            int boxr = p.BS < win ? p.BS : win;
             const long long tokens = p.NB * p.BS;
             if (!encode_cache_map(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) ||
                 !encode_cache_map(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
@@ -1220,10 +1748,10 @@ size_t varlen_workspace_size(const dvattn_varlen_args* v) {
     dvattn_paged_args a = varlen_as_paged(v);
     if (decode_validate(&a) != DVATTN_OK) return 0;
     KernelChoice kc;
-    choose(a.dtype, a.E, a.block_size, a.num_blocks, kc);
+    choose(a.dtype, a.E, a.Hkv, a.block_size, a.num_blocks, kc);
     int n_launch = 0;
     if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
-    return decode_layout(v->T, v->E, n_launch, true).total;
+    return decode_layout(v->T, v->E, n_launch, true, kc.row ? v->Hkv : 1).total;
 }
 
 int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, cudaStream_t stream) {

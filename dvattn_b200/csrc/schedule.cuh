@@ -1,7 +1,8 @@
 // Balanced split-KV schedule shared by the paged-decode kernels and their merge.
 //
-// Work unit = one visible key token of one (query row, KV head) "segment".  Segment
-// g = ws * Hkv + hkv, where ws = w * S + s indexes the query rows of the paged op.
+// Work unit = one visible key token of one (query row, KV head) "segment" (or of one
+// query row with all its KV heads, when hsplit == 1).  Segment g = ws * Hkv + hkv, where
+// ws = w * S + s indexes the query rows of the paged op.
 // The visible keys of a segment are the concatenation over turns f of the keys
 // l < V_f(ws) = min(L_f, loc[f,ws] + 1) (clipped to the block table), so masked turn
 // padding is never scheduled.  Units are ordered segment-major; with P[ws] the
@@ -55,6 +56,11 @@ struct PagedParams {
     int nseq;
     int* row_seq;      // [WS] workspace, valid when cu_q != null
     int cs_stride;     // floats per cos/sin row: R (decode) or R/2 (varlen)
+    // Unit ordering: a row's visible keys form `hsplit` segments (one per KV head, hsplit
+    // = Hkv) for kernels that stream one head per CTA, or one segment covering all heads
+    // (hsplit = 1) for the row kernel; a partial slot holds `slot_heads` heads.
+    int hsplit;
+    int slot_heads;
 };
 
 __device__ __forceinline__ int row_block_table(const PagedParams& p, int ws) {
@@ -139,7 +145,7 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
     if (tid == 0) {
         const long long tot = carry_s;
         p.P[p.WS] = tot;
-        const long long U = tot * p.Hkv;
+        const long long U = tot * p.hsplit;
         long long want = (U + p.min_units - 1) / p.min_units;
         int n = (int)(want < p.n_launch ? want : p.n_launch);
         p.sched->U = U;
@@ -156,13 +162,15 @@ struct TileDesc {
     bool new_seg, new_turn, seg_last, seg_complete, first_piece;
 };
 
-// ALIGN: tiles also never cross a TILE-aligned window of logical positions (so a tile's
-// rows map to fixed window rows, as the TMA kernel's page boxes need).
-template <int TILE, bool ALIGN = false> struct TileIter {
+// With `align` > 0 (a power of two <= TILE) tiles also never cross an align-sized window
+// of logical positions, so a tile's keys sit at fixed window rows, as the TMA kernels'
+// page boxes need.
+template <int TILE> struct TileIter {
     int ws, hkv, f, t, off, vis;
     long long rem;
     int seg_left;
     bool from_start, pend_seg, pend_turn, first_seg;
+    int align;
 
     __device__ __forceinline__ int seg_len(const PagedParams& p, int w) const {
         return (int)(p.P[w + 1] - p.P[w]);
@@ -172,7 +180,7 @@ template <int TILE, bool ALIGN = false> struct TileIter {
     __device__ __forceinline__ void init(const PagedParams& p, int ws0, long long u0, long long u1) {
         ws = ws0;
         const int V = seg_len(p, ws);
-        long long r = u0 - p.P[ws] * p.Hkv;
+        long long r = u0 - p.P[ws] * p.hsplit;
         hkv = (int)(r / V);
         int ts = (int)(r - (long long)hkv * V);
         seg_left = V - ts;
@@ -190,6 +198,7 @@ template <int TILE, bool ALIGN = false> struct TileIter {
         rem = u1 - u0;
         pend_seg = pend_turn = true;
         first_seg = true;
+        align = 0;
     }
 
     __device__ __forceinline__ bool next(const PagedParams& p, TileDesc& d) {
@@ -202,7 +211,7 @@ template <int TILE, bool ALIGN = false> struct TileIter {
             if (f == p.F) {
                 f = 0;
                 off = 0;
-                if (++hkv == p.Hkv) {
+                if (++hkv == p.hsplit) {
                     hkv = 0;
                     do { ++ws; } while (p.P[ws + 1] == p.P[ws]);
                 }
@@ -215,8 +224,8 @@ template <int TILE, bool ALIGN = false> struct TileIter {
         }
         int n = vis - t;
         if (n > TILE) n = TILE;
-        if (ALIGN) {
-            const int room = TILE - ((off + t) & (TILE - 1));
+        if (align) {
+            const int room = align - ((off + t) & (align - 1));
             if (n > room) n = room;
         }
         if ((long long)n > rem) n = (int)rem;
@@ -245,7 +254,7 @@ __device__ __forceinline__ int find_row(const PagedParams& p, long long u0) {
     int cnt = 0;
     for (int base = 0; base < p.WS; base += NT) {
         const int i = base + (int)threadIdx.x;
-        const int pred = (i < p.WS) && (p.P[i] * p.Hkv <= u0);
+        const int pred = (i < p.WS) && (p.P[i] * p.hsplit <= u0);
         const int c = __syncthreads_count(pred);
         cnt += c;
         if (c < NT) break;

@@ -198,3 +198,30 @@ def test_torch_op_errors():
     with pytest.raises(RuntimeError, match="not part of the B200 build"):
         torch.ops.libdvatt.dvattn_sdpa(c.new_out(), 0.1, c.locations, c.queries, c.fragment_lengths, [c.k_cache],
                                        [c.v_cache])
+
+
+@pytest.mark.parametrize("Hkv", [1, 2, 3, 4, 8, 16])
+@pytest.mark.parametrize("BS", [8, 16, 64, 128])
+def test_kv_head_counts_and_pages(Hkv, BS):
+    """Covers the row kernel (Hkv in 1,2,4,8), the per-head TMA kernel (other Hkv) and the
+    page-size windows of both."""
+    c = wl.make_paged([[700, 90], [33, 400], [5, 0]], Hq=4 * Hkv, Hkv=Hkv, E=128, R=64, BS=BS,
+                      dtype=torch.bfloat16, seed=Hkv * 100 + BS)
+    check_vs_oracle(c, f"Hkv={Hkv} BS={BS}")
+
+
+def test_config3_shape_subset():
+    """Config 3 head layout (128/8, E=128, full rotary, page 64) on a shorter context."""
+    c = wl.make_paged([[20000]] * 2, Hq=128, Hkv=8, E=128, R=128, BS=64, dtype=torch.float16, seed=3)
+    check_vs_oracle(c, "config3 shape")
+
+
+def test_error_flag_clear_after_calls():
+    """The bounded waits never gave up: the workspace header's error word stays 0."""
+    c = wl.config2(W=4).to(DEV)
+    out = c.new_out()
+    call = capi.PagedCall(*c.op_args(out))
+    call()
+    torch.cuda.synchronize()
+    hdr = call.workspace[:16].cpu().view(torch.int32)
+    assert int(hdr[3]) == 0  # {U (int64), n_eff, error}
