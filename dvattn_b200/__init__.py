@@ -21,7 +21,7 @@ CAPI_LIB = os.path.join(_HERE, "libdvattn_b200.so")
 def _load() -> None:
     if not os.path.exists(TORCH_OPS_LIB) or not os.path.exists(CAPI_LIB):
         raise ImportError(
-            "dvattn_b200: native libraries not built (expected %s and %s); run `python -m dvattn_b200._build`"
+            "dvattn_b200: native libraries not built (expected %s and %s); run `python dvattn_b200/_build.py`"
             % (CAPI_LIB, TORCH_OPS_LIB))
     torch.ops.load_library(TORCH_OPS_LIB)
 

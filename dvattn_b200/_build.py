@@ -5,7 +5,7 @@
 * ``dvatt.abi3.so``    -- the ``torch.ops.libdvatt`` registration (same file name as the
   reference extension), a thin C++ layer over the C ABI linked against torch.
 
-Run ``python -m dvattn_b200._build`` (or ``__graft_entry__.build()``).  Outputs land next to
+Run ``python dvattn_b200/_build.py`` (or ``__graft_entry__.build()``).  Outputs land next to
 this file; sources are rebuilt only when newer than their outputs.
 """
 from __future__ import annotations

@@ -40,7 +40,7 @@ __device__ __forceinline__ float rotated_elem(const T* qrow, const float* cr, co
 // owns a chunk of 8 rotary pairs (chunks c and c + R/16), or one pass-through chunk.
 template <class T, int E, int MAXT>
 __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int f, int h0, int nh, uint8_t* sQ, int tid,
-                                              int nth) {
+                                              int nth, float* sCS, int bar_id) {
     constexpr int CH = E / 8;
     const int w = ws / p.S, s = ws - w * p.S;
     const float* cr = p.cos + ((size_t)f * p.WS + ws) * p.cs_stride;
@@ -58,6 +58,11 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
         const int npair = hp >> 3, npass = (E - R) >> 3;
         const int per_row = npair + npass;
         const int ntask = nh * 16 * per_row;
+        // one round of loads: the cos/sin rows into sCS, the q chunks into registers
+        for (int k = tid; k < 2 * (hp >> 2); k += nth) {
+            const int half = k / (hp >> 2), jj = k - half * (hp >> 2);
+            reinterpret_cast<float4*>(sCS + half * hp)[jj] = reinterpret_cast<const float4*>(half ? sr : cr)[jj];
+        }
         uint4 a[MAXT], b[MAXT];
 #pragma unroll
         for (int k = 0; k < MAXT; ++k) {
@@ -76,6 +81,7 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
                 }
             }
         }
+        named_bar_sync(bar_id, nth);
 #pragma unroll
         for (int k = 0; k < MAXT; ++k) {
             const int t = tid + k * nth;
@@ -84,10 +90,10 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
             if (j < npair) {
                 const T* x = reinterpret_cast<const T*>(&a[k]);
                 const T* y = reinterpret_cast<const T*>(&b[k]);
-                const float4 c0 = *reinterpret_cast<const float4*>(cr + j * 8);
-                const float4 c1 = *reinterpret_cast<const float4*>(cr + j * 8 + 4);
-                const float4 s0 = *reinterpret_cast<const float4*>(sr + j * 8);
-                const float4 s1 = *reinterpret_cast<const float4*>(sr + j * 8 + 4);
+                const float4 c0 = reinterpret_cast<const float4*>(sCS + j * 8)[0];
+                const float4 c1 = reinterpret_cast<const float4*>(sCS + j * 8)[1];
+                const float4 s0 = reinterpret_cast<const float4*>(sCS + hp + j * 8)[0];
+                const float4 s1 = reinterpret_cast<const float4*>(sCS + hp + j * 8)[1];
                 const float cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
                 const float ss[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
                 uint32_t lo[4], hi[4];
@@ -117,6 +123,34 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
                 }
             }
             *dst(row, ch) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+    }
+}
+
+// L2 prefetch of what rotate_q_rows will read for (ws, f): the q rows of all heads and
+// the cos/sin rows (bulk prefetch wants 16-byte aligned, 16-byte multiple ranges).
+template <class T, int E>
+__device__ __forceinline__ void prefetch_rotation_inputs(const PagedParams& p, int ws, int f, int lane) {
+    const int w = ws / p.S, s = ws - w * p.S;
+    if (p.S == 1) {
+        if (lane == 0) {
+            const T* q = static_cast<const T*>(p.q) + (size_t)w * p.Hq * E;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"((uint32_t)(p.Hq * E * sizeof(T)))
+                         : "memory");
+        }
+    } else {
+        for (int hq = lane; hq < p.Hq; hq += 32) {
+            const T* q = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"((uint32_t)(E * sizeof(T))) : "memory");
+        }
+    }
+    const int hp = p.R >> 1;
+    if (lane == 1 && hp > 0 && (hp & 3) == 0) {
+        const float* cr = p.cos + ((size_t)f * p.WS + ws) * p.cs_stride;
+        const float* sr = p.sin + ((size_t)f * p.WS + ws) * p.cs_stride;
+        if (((reinterpret_cast<uintptr_t>(cr) | reinterpret_cast<uintptr_t>(sr)) & 15) == 0) {
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(cr), "r"((uint32_t)(hp * 4)) : "memory");
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sr), "r"((uint32_t)(hp * 4)) : "memory");
         }
     }
 }
@@ -429,10 +463,11 @@ struct TmaCfg {
     static constexpr size_t OFF_Q = 2 * OFF_V;
     static constexpr size_t OFF_O = OFF_Q + 16 * 2 * E;
     static constexpr size_t OFF_ML = OFF_O + 16 * E * 4;
-    static constexpr size_t OFF_LSE = OFF_ML + CW * 16 * 2 * 4;
+    static constexpr size_t OFF_LSE = OFF_ML + (CW * 16 * 2 > E ? CW * 16 * 2 : E) * 4;
     static constexpr size_t OFF_DESC = OFF_LSE + 16 * 4;
     static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
     static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
+    static constexpr size_t OFF_CS = OFF_ML;  // cos/sin staging of a rotation aliases the merge stats
     static constexpr size_t SMEM = OFF_FLAG + 16;
 };
 
@@ -590,7 +625,8 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
         }
         if (d.flags & 2) {
             named_bar_sync(2, CW * 32);
-            rotate_q_rows<T, E, (16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, d.hkv, 1, sQ, tid, CW * 32);
+            rotate_q_rows<T, E, (16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, d.hkv, 1, sQ, tid, CW * 32,
+                                                                         reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -794,10 +830,11 @@ struct RowCfg {
     // turn change and the merge buffer only at a row's end, so the two share memory.
     static constexpr size_t OFF_O = QREG ? OFF_Q : OFF_Q + QBYTES;
     static constexpr size_t OFF_ML = QREG ? OFF_Q + (QBYTES > OBYTES ? QBYTES : OBYTES) : OFF_O + OBYTES;
-    static constexpr size_t OFF_LSE = OFF_ML + CW * 16 * 2 * 4;
+    static constexpr size_t OFF_LSE = OFF_ML + (CW * 16 * 2 > E ? CW * 16 * 2 : E) * 4;
     static constexpr size_t OFF_DESC = OFF_LSE + 2 * 16 * 4;
     static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
     static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
+    static constexpr size_t OFF_CS = OFF_ML;  // cos/sin staging of a rotation aliases the merge stats
     static constexpr size_t SMEM = OFF_FLAG + 16;
 };
 
@@ -826,7 +863,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int Hkv = p.Hkv;
     const int TOKB = (CW / Hkv) * 16;           // keys per stage (window)
-    const int SLAB = TOKB * 128;                // bytes of one (head, panel) slab
+    // One TMA box = one page (or the window's part of it) for all heads and panels:
+    // smem [page chunk][head][panel][boxr rows][128 B].
+    const int boxr_shift = __ffs(boxr) - 1;
+    const uint32_t box_bytes = (uint32_t)Hkv * NPANEL * boxr * 128u;
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
@@ -853,12 +893,37 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         TileIter<64> it;
         it.init(p, ws0, u0, u1);
         it.align = TOKB;
-        const uint32_t box_bytes = (uint32_t)boxr * 128u;
+        struct Pend {
+            TileDesc d;
+            int pfirst, npg, page;
+            bool have;
+        };
+        // next tile: descriptor, its pages, and (lane j) the block-table entry of page j;
+        // prepared one tile ahead so the table load is in flight during the stage wait.
+        auto prep = [&](Pend& q) {
+            q.have = it.next(p, q.d);
+            if (!q.have) return;
+            const int pos0 = q.d.pos0;
+            if (p.BS <= TOKB) {
+                const int last = pos0 + q.d.n - 1;
+                q.pfirst = p.bs_shift >= 0 ? pos0 >> p.bs_shift : pos0 / p.BS;
+                q.npg = (p.bs_shift >= 0 ? last >> p.bs_shift : last / p.BS) - q.pfirst + 1;
+            } else {
+                const int win = pos0 & ~(TOKB - 1);
+                q.pfirst = p.bs_shift >= 0 ? win >> p.bs_shift : win / p.BS;
+                q.npg = 1;
+            }
+            const int btrow = p.cu_q ? p.row_seq[q.d.ws] : (p.S == 1 ? q.d.ws : q.d.ws / p.S);
+            q.page = lane < q.npg ? __ldg(p.bt + (size_t)btrow * p.maxb + q.pfirst + lane) : 0;
+            if (q.d.new_turn) prefetch_rotation_inputs<T, E>(p, q.d.ws, q.d.f, lane);
+        };
+        Pend cur, nxt;
+        prep(nxt);
         int i = 0;
         bool ok = true;
         for (;; ++i) {
-            TileDesc d;
-            const bool have = it.next(p, d);
+            cur = nxt;
+            if (cur.have) prep(nxt);
             const int st = i % STAGES;
             if (i >= STAGES && !*sAbort) {
                 if (!mbar_wait(bar_empty + st * 8, ((i / STAGES) & 1) ^ 1)) {
@@ -866,26 +931,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                     break;
                 }
             }
-            if (!have) {
+            if (!cur.have) {
                 if (lane == 0) {
                     sDesc[st].n = -1;
                     mbar_arrive(bar_full + st * 8);
                 }
                 break;
             }
+            const TileDesc& d = cur.d;
             const int win = d.pos0 & ~(TOKB - 1);
-            int pfirst, npg;
-            if (p.BS <= TOKB) {
-                pfirst = d.pos0 / p.BS;
-                npg = (d.pos0 + d.n - 1) / p.BS - pfirst + 1;
-            } else {
-                pfirst = win / p.BS;
-                npg = 1;
-            }
-            const int ntask = npg * Hkv;  // (page, head) pairs, <= 32
-            const int pg = lane / Hkv, hh = lane - pg * Hkv;
-            const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
-            const int page = lane < ntask ? __ldg(btw + pfirst + pg) : 0;
             if (lane == 0) {
                 StageDesc sd;
                 sd.ws = d.ws;
@@ -896,25 +950,23 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                 sd.flags = (d.new_seg ? 1 : 0) | (d.new_turn ? 2 : 0) | (d.seg_last ? 4 : 0) |
                            (d.seg_complete ? 8 : 0) | (d.first_piece ? 16 : 0);
                 sDesc[st] = sd;
-                mbar_expect_tx(bar_full + st * 8, (uint32_t)ntask * NPANEL * 2u * box_bytes);
+                mbar_expect_tx(bar_full + st * 8, (uint32_t)cur.npg * 2u * box_bytes);
             }
             __syncwarp();
-            if (lane < ntask) {
-                int z, srow;
+            if (lane < cur.npg) {
+                const int page = cur.page;
                 const bool valid = p.NB <= 0 || (page >= 0 && page < p.NB);
+                int z, chunk;
                 if (p.BS <= TOKB) {
                     z = valid ? page * p.BS : -2 * boxr;
-                    srow = (pfirst + pg) * p.BS - win;
+                    chunk = ((cur.pfirst + lane) * p.BS - win) >> boxr_shift;
                 } else {
-                    z = valid ? page * p.BS + (win - pfirst * p.BS) : -2 * boxr;
-                    srow = 0;
+                    z = valid ? page * p.BS + (win - cur.pfirst * p.BS) : -2 * boxr;
+                    chunk = 0;
                 }
-                const uint32_t off = (uint32_t)(st * C::STAGE_BYTES + hh * NPANEL * SLAB + srow * 128);
-#pragma unroll
-                for (int pn = 0; pn < NPANEL; ++pn) {
-                    tma_load_3d(sK0 + off + pn * SLAB, &tmk, pn * 64, hh, z, bar_full + st * 8);
-                    tma_load_3d(sV0 + off + pn * SLAB, &tmv, pn * 64, hh, z, bar_full + st * 8);
-                }
+                const uint32_t off = (uint32_t)(st * C::STAGE_BYTES) + (uint32_t)chunk * box_bytes;
+                tma_load_4d(sK0 + off, &tmk, 0, z, 0, 0, bar_full + st * 8);
+                tma_load_4d(sV0 + off, &tmv, 0, z, 0, 0, bar_full + st * 8);
             }
         }
         if (!ok) {
@@ -937,6 +989,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     float m0 = 0.f, m1 = 0.f, l0 = 0.f, l1 = 0.f;
     const float sl2 = p.scale_log2;
     const uint32_t qh = sQ0 + h * NPANEL * 2048;
+    // byte offset of 16-byte chunk `ch` of key row `row` of head h in a K/V stage
+    auto kv_off = [&](int row, int ch) -> uint32_t {
+        return (uint32_t)((((row >> boxr_shift) * Hkv + h) * NPANEL + (ch >> 3)) * boxr + (row & (boxr - 1))) * 128u +
+               (uint32_t)(((ch & 7) ^ (row & 7)) << 4);
+    };
     for (int i = 0;; ++i) {
         if (named_bar_or(1, CW * 32, *sAbort != 0)) break;
         const int st = i % STAGES;
@@ -957,7 +1014,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         }
         if (d.flags & 2) {
             named_bar_sync(2, CW * 32);
-            rotate_q_rows<T, E, (CW * 16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, 0, Hkv, sQ, tid, CW * 32);
+            rotate_q_rows<T, E, (CW * 16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, 0, Hkv, sQ, tid, CW * 32,
+                                                                           reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -970,17 +1028,16 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         }
 
         const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
-        const uint32_t kb = sK0 + st * C::STAGE_BYTES + h * NPANEL * SLAB;
-        const uint32_t vb = sV0 + st * C::STAGE_BYTES + h * NPANEL * SLAB;
+        const uint32_t kb = sK0 + st * C::STAGE_BYTES;
+        const uint32_t vb = sV0 + st * C::STAGE_BYTES;
         if (hi > lo) {
             const bool edge = (lo > 0) || (hi < 16);
             if (edge) {
-                uint8_t* vrow = smem + C::OFF_V + (size_t)st * C::STAGE_BYTES + (size_t)h * NPANEL * SLAB;
+                uint8_t* vst = smem + C::OFF_V + (size_t)st * C::STAGE_BYTES;
                 for (int idx = lane; idx < 16 * NPANEL * 8; idx += 32) {
                     const int j = idx / (NPANEL * 8), rem = idx % (NPANEL * 8);
                     if (j < lo || j >= hi)
-                        *reinterpret_cast<uint4*>(vrow + (rem >> 3) * SLAB + (rb + j) * 128 + (rem & 7) * 16) =
-                            make_uint4(0u, 0u, 0u, 0u);
+                        *reinterpret_cast<uint4*>(vst + kv_off(rb + j, rem)) = make_uint4(0u, 0u, 0u, 0u);
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
@@ -997,7 +1054,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                 }
                 const int ch = kk * 2 + ((lane >> 3) & 1), row = rb + (lane & 7) + ((lane >> 4) << 3);
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4(kb + (ch >> 3) * SLAB + row * 128 + (((ch & 7) ^ (row & 7)) << 4), b0, b1, b2, b3);
+                ldsm_x4(kb + kv_off(row, ch), b0, b1, b2, b3);
                 Mma<T>::run(sc[0], a, b0, b1);
                 Mma<T>::run(sc[1], a, b2, b3);
             }
@@ -1049,7 +1106,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             for (int np = 0; np < E / 16; ++np) {
                 const int ch = 2 * np + (lane >> 4), row = rb + (lane & 7) + (((lane >> 3) & 1) << 3);
                 uint32_t b0, b1, b2, b3;
-                ldsm_x4_t(vb + (ch >> 3) * SLAB + row * 128 + (((ch & 7) ^ (row & 7)) << 4), b0, b1, b2, b3);
+                ldsm_x4_t(vb + kv_off(row, ch), b0, b1, b2, b3);
                 Mma<T>::run(o[2 * np], pa, b0, b1);
                 Mma<T>::run(o[2 * np + 1], pa, b2, b3);
             }
@@ -1382,6 +1439,17 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
 // merge of split segments (and zeros for rows that see no key)
 // one CTA per segment, 128 threads: thread t -> row t/8, columns 4*((t%8) + 8k)
 // ==================================================================================
+// four consecutive output elements (8-byte store for 16-bit types, 16-byte for f32)
+template <class T> __device__ __forceinline__ void store_quad(T* dst, float a, float b, float c, float d) {
+    uint2 pk;
+    pk.x = Elem<T>::pack2(a, b);
+    pk.y = Elem<T>::pack2(c, d);
+    *reinterpret_cast<uint2*>(dst) = pk;
+}
+template <> __device__ __forceinline__ void store_quad<float>(float* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+}
+
 template <class T>
 __global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E) {
     const int g_seg = blockIdx.x;
@@ -1406,40 +1474,54 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E)
     const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
     const int n = sch.n_eff;
     const int ca = cta_of(b, sch.U, n), cb = cta_of(b + V - 1, sch.U, n);
-    if (ca == cb || r >= p.gqa) return;
+    if (ca == cb) return;
+    // partial-record index of every piece, computed once per batch of 128 pieces (the
+    // int64 divisions of cta_start are not repeated per thread)
+    __shared__ int s_part[128];
+    const int npc = cb - ca + 1;
     const int hh = p.slot_heads > 1 ? hkv : 0;
-    auto part = [&](int c) {
-        const int slot = (c == ca && cta_start(ca, sch.U, n) < b) ? 2 * ca + 1 : 2 * c;
-        return (slot * p.slot_heads + hh) * 16 + r;
-    };
-
-    float lmax = neg_inf();
-    for (int c = ca; c <= cb; ++c) lmax = fmaxf(lmax, p.part_lse[part(c)]);
+    const bool ca_not_first = cta_start(ca, sch.U, n) < b;
     float acc[32];
     const int nchunk = E / 32;  // float4 chunks per thread
     for (int j = 0; j < 4 * nchunk; ++j) acc[j] = 0.f;
-    float den = 0.f;
-    for (int c = ca; c <= cb; ++c) {
-        const int pi = part(c);
-        const float ls = p.part_lse[pi];
-        if (ls == neg_inf()) continue;
-        const float wgt = fast_exp2(ls - lmax);
-        den += wgt;
-        const float* po = p.part_o + (size_t)pi * E;
-        for (int j = 0; j < nchunk; ++j) {
-            const float4 v = *reinterpret_cast<const float4*>(po + 4 * (sub + 8 * j));
-            acc[4 * j + 0] += wgt * v.x;
-            acc[4 * j + 1] += wgt * v.y;
-            acc[4 * j + 2] += wgt * v.z;
-            acc[4 * j + 3] += wgt * v.w;
+    float lmax = neg_inf(), den = 0.f;
+    for (int base = 0; base < npc; base += 128) {
+        const int cnt = min(128, npc - base);
+        __syncthreads();
+        if (tid < cnt) {
+            const int cc = ca + base + tid;
+            const int slot = (cc == ca && ca_not_first) ? 2 * ca + 1 : 2 * cc;
+            s_part[tid] = (slot * p.slot_heads + hh) * 16;
+        }
+        __syncthreads();
+        if (r >= p.gqa) continue;
+        // online merge; the unrolled loop keeps several pieces' loads in flight
+#pragma unroll 4
+        for (int k = 0; k < cnt; ++k) {
+            const int pi = s_part[k] + r;
+            const float ls = p.part_lse[pi];
+            if (ls == neg_inf()) continue;
+            const float* po = p.part_o + (size_t)pi * E;
+            float4 v[8];
+            for (int j = 0; j < nchunk; ++j) v[j] = *reinterpret_cast<const float4*>(po + 4 * (sub + 8 * j));
+            const float nm = fmaxf(lmax, ls);
+            const float sa = fast_exp2(lmax - nm), sb = fast_exp2(ls - nm);
+            den = den * sa + sb;
+            for (int j = 0; j < nchunk; ++j) {
+                acc[4 * j + 0] = acc[4 * j + 0] * sa + sb * v[j].x;
+                acc[4 * j + 1] = acc[4 * j + 1] * sa + sb * v[j].y;
+                acc[4 * j + 2] = acc[4 * j + 2] * sa + sb * v[j].z;
+                acc[4 * j + 3] = acc[4 * j + 3] * sa + sb * v[j].w;
+            }
+            lmax = nm;
         }
     }
+    if (r >= p.gqa) return;
     const float inv = den > 0.f ? 1.f / den : 0.f;
     T* op = static_cast<T*>(p.out) + orow * E;
     for (int j = 0; j < nchunk; ++j) {
         const int e = 4 * (sub + 8 * j);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) op[e + q] = Elem<T>::from_f(acc[4 * j + q] * inv);
+        store_quad<T>(op + e, acc[4 * j] * inv, acc[4 * j + 1] * inv, acc[4 * j + 2] * inv, acc[4 * j + 3] * inv);
         if (p.out_f32)
             *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) =
                 make_float4(acc[4 * j] * inv, acc[4 * j + 1] * inv, acc[4 * j + 2] * inv, acc[4 * j + 3] * inv);
@@ -1539,6 +1621,24 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 // [tokens = NB*BS][Hkv][E] cache as a 3-D map, box = 64 columns x 1 head x boxr tokens,
 // 128-byte swizzle.
+// [tokens][Hkv][E] cache as a 4-D map {64 columns, tokens, E/64 panels, Hkv heads} whose box
+// {64, boxr, E/64, Hkv} is one page for all heads, landing as [head][panel][row][128 B]
+// with the 128-byte swizzle.
+bool encode_cache_map_all_heads(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long tokens,
+                                int boxr) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    cuuint64_t dims[4] = {64, (cuuint64_t)tokens, (cuuint64_t)(E / 64), (cuuint64_t)Hkv};
+    cuuint64_t strides[3] = {(cuuint64_t)Hkv * E * 2, 128, (cuuint64_t)E * 2};
+    cuuint32_t box[4] = {64, (cuuint32_t)boxr, (cuuint32_t)(E / 64), (cuuint32_t)Hkv};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    const CUtensorMapDataType dt =
+        dtype == DVATTN_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    return fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_cache_map(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long tokens, int boxr) {
     auto fn = tensor_map_encoder();
     if (!fn) return false;
@@ -1658,6 +1758,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     int st = device_sms_and_occ(kc, n_launch);
     if (st != DVATTN_OK) return st;
     p.hsplit = kc.row ? 1 : p.Hkv;
+    p.bs_shift = (p.BS & (p.BS - 1)) == 0 ? __builtin_ctz((unsigned)p.BS) : -1;
     p.slot_heads = kc.row ? p.Hkv : 1;
     const DecodeLayout L = decode_layout(p.WS, p.E, n_launch, p.cu_q != nullptr, p.slot_heads);
     if (!workspace || wbytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255)) return DVATTN_ERR_WORKSPACE;
@@ -1677,8 +1778,8 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
             const int win = kc.row ? 16 * kc.cw / p.Hkv : 64;
             int boxr = p.BS < win ? p.BS : win;
             const long long tokens = p.NB * p.BS;
-            if (!encode_cache_map(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) ||
-                !encode_cache_map(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
+            auto enc = kc.row ? encode_cache_map_all_heads : encode_cache_map;
+            if (!enc(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) || !enc(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
                 return DVATTN_ERR_CUDA;
             void* args[] = {&p, &mk, &mv, &boxr};
             if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)

@@ -61,6 +61,7 @@ struct PagedParams {
     // (hsplit = 1) for the row kernel; a partial slot holds `slot_heads` heads.
     int hsplit;
     int slot_heads;
+    int bs_shift;      // log2(block_size) when it is a power of two, else -1
 };
 
 __device__ __forceinline__ int row_block_table(const PagedParams& p, int ws) {
