@@ -40,6 +40,8 @@ EXPORTS = [
     "dvattn_paged_sdpa_workspace_size",
     "dvattn_paged_sdpa",
     "dvattn_paged_sdpa_phase",
+    "dvattn_paged_sdpa_noalloc_max_workspace",
+    "dvattn_paged_sdpa_noalloc",
     "dvattn_varlen_paged_sdpa_workspace_size",
     "dvattn_varlen_paged_sdpa",
     "dvattn_rope",
@@ -87,6 +89,10 @@ def lib() -> ctypes.CDLL:
         L.dvattn_paged_sdpa.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _vp]
         L.dvattn_paged_sdpa_phase.restype = _i
         L.dvattn_paged_sdpa_phase.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _i, _vp]
+        L.dvattn_paged_sdpa_noalloc_max_workspace.restype = ctypes.c_size_t
+        L.dvattn_paged_sdpa_noalloc_max_workspace.argtypes = []
+        L.dvattn_paged_sdpa_noalloc.restype = _i
+        L.dvattn_paged_sdpa_noalloc.argtypes = [ctypes.POINTER(PagedArgs), _vp]
         L.dvattn_varlen_paged_sdpa_workspace_size.restype = ctypes.c_size_t
         L.dvattn_varlen_paged_sdpa_workspace_size.argtypes = [ctypes.POINTER(VarlenArgs)]
         L.dvattn_varlen_paged_sdpa.restype = _i

@@ -137,6 +137,22 @@ int dvattn_paged_sdpa(const dvattn_paged_args* args, void* workspace, size_t wor
 int dvattn_paged_sdpa_phase(const dvattn_paged_args* args, void* workspace, size_t workspace_bytes, int phase,
                             dvattn_stream_t stream);
 
+/*
+ * dvattn_paged_sdpa without a caller-supplied workspace, for callers that cannot allocate
+ * device memory (an engine whose pool owns all of the GPU's memory and forbids
+ * cudaMalloc after start-up, or a plain C host with no device allocator).  No
+ * counterpart in the reference.  The split-KV scratch is one fixed array of
+ * dvattn_paged_sdpa_noalloc_max_workspace() bytes (32 MiB) inside the library, held on
+ * every GPU that loads it until the process exits; this entry point calls no
+ * cudaMalloc/cudaFree.  Problems whose dvattn_paged_sdpa_workspace_size() exceeds that
+ * return DVATTN_ERR_WORKSPACE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress); make that first call before any stream capture.  All
+ * calls on one device share the array, so calls that may overlap on the GPU (different
+ * streams without ordering) race: serialise them.
+ */
+size_t dvattn_paged_sdpa_noalloc_max_workspace(void);
+int dvattn_paged_sdpa_noalloc(const dvattn_paged_args* args, dvattn_stream_t stream);
+
 /* Workspace bytes of dvattn_varlen_paged_sdpa (see dvattn_paged_sdpa_workspace_size). */
 size_t dvattn_varlen_paged_sdpa_workspace_size(const dvattn_varlen_args* args);
 
