@@ -13,6 +13,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 namespace dvb {
 
 // ----------------------------------------------------------------------------------
@@ -1450,24 +1452,26 @@ template <> __device__ __forceinline__ void store_quad<float>(float* dst, float 
     *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
 }
 
-template <class T>
-__global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E) {
+// One block per segment (ws, hkv), one thread per (query row r, 4-column group c4):
+// blockDim = 16 * E / 4.  Pieces are consumed in batches of 8 whose loads are all in
+// flight before any is used (the merge is latency-bound, not bandwidth-bound).
+template <class T, int E>
+__global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p) {
+    constexpr int C4 = E / 4, NTH = 16 * C4, B = 8;
+    // launched as a programmatic dependent of the attention kernel: wait for its results
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int g_seg = blockIdx.x;
     const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
-    const int tid = threadIdx.x, r = tid >> 3, sub = tid & 7;
+    const int tid = threadIdx.x, r = tid / C4, c4 = tid - r * C4;
     const DecodeSched sch = *p.sched;
     const long long P0 = p.P[ws], V = p.P[ws + 1] - P0;
     const int w = ws / p.S, s = ws - w * p.S;
     const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
     if (V == 0) {
         if (r < p.gqa) {
-            T* op = static_cast<T*>(p.out) + orow * E;
-            for (int e = 4 * sub; e < E; e += 32) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) op[e + j] = Elem<T>::from_f(0.f);
-                if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
-            if (p.lse_out && sub == 0) p.lse_out[orow] = neg_inf();
+            store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, 0.f, 0.f, 0.f, 0.f);
+            if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p.lse_out && c4 == 0) p.lse_out[orow] = neg_inf();
         }
         return;
     }
@@ -1475,18 +1479,14 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E)
     const int n = sch.n_eff;
     const int ca = cta_of(b, sch.U, n), cb = cta_of(b + V - 1, sch.U, n);
     if (ca == cb) return;
-    // partial-record index of every piece, computed once per batch of 128 pieces (the
-    // int64 divisions of cta_start are not repeated per thread)
-    __shared__ int s_part[128];
+    __shared__ int s_part[NTH];
     const int npc = cb - ca + 1;
     const int hh = p.slot_heads > 1 ? hkv : 0;
     const bool ca_not_first = cta_start(ca, sch.U, n) < b;
-    float acc[32];
-    const int nchunk = E / 32;  // float4 chunks per thread
-    for (int j = 0; j < 4 * nchunk; ++j) acc[j] = 0.f;
-    float lmax = neg_inf(), den = 0.f;
-    for (int base = 0; base < npc; base += 128) {
-        const int cnt = min(128, npc - base);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float M = neg_inf(), den = 0.f;
+    for (int base = 0; base < npc; base += NTH) {
+        const int cnt = min(NTH, npc - base);
         __syncthreads();
         if (tid < cnt) {
             const int cc = ca + base + tid;
@@ -1495,38 +1495,41 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(PagedParams p, int E)
         }
         __syncthreads();
         if (r >= p.gqa) continue;
-        // online merge; the unrolled loop keeps several pieces' loads in flight
-#pragma unroll 4
-        for (int k = 0; k < cnt; ++k) {
-            const int pi = s_part[k] + r;
-            const float ls = p.part_lse[pi];
-            if (ls == neg_inf()) continue;
-            const float* po = p.part_o + (size_t)pi * E;
-            float4 v[8];
-            for (int j = 0; j < nchunk; ++j) v[j] = *reinterpret_cast<const float4*>(po + 4 * (sub + 8 * j));
-            const float nm = fmaxf(lmax, ls);
-            const float sa = fast_exp2(lmax - nm), sb = fast_exp2(ls - nm);
-            den = den * sa + sb;
-            for (int j = 0; j < nchunk; ++j) {
-                acc[4 * j + 0] = acc[4 * j + 0] * sa + sb * v[j].x;
-                acc[4 * j + 1] = acc[4 * j + 1] * sa + sb * v[j].y;
-                acc[4 * j + 2] = acc[4 * j + 2] * sa + sb * v[j].z;
-                acc[4 * j + 3] = acc[4 * j + 3] * sa + sb * v[j].w;
+        for (int k0 = 0; k0 < cnt; k0 += B) {
+            float l[B];
+            float4 v[B];
+#pragma unroll
+            for (int j = 0; j < B; ++j) {
+                l[j] = neg_inf();
+                v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k0 + j < cnt) {
+                    const int pi = s_part[k0 + j] + r;
+                    l[j] = p.part_lse[pi];
+                    v[j] = reinterpret_cast<const float4*>(p.part_o + (size_t)pi * E)[c4];
+                }
             }
-            lmax = nm;
+            float mb = M;
+#pragma unroll
+            for (int j = 0; j < B; ++j) mb = fmaxf(mb, l[j]);
+            if (mb == neg_inf()) continue;
+            const float sc = fast_exp2(M - mb);
+            den *= sc;
+            acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+#pragma unroll
+            for (int j = 0; j < B; ++j) {
+                const float wj = fast_exp2(l[j] - mb);  // 0 for empty pieces
+                den += wj;
+                acc.x += wj * v[j].x; acc.y += wj * v[j].y; acc.z += wj * v[j].z; acc.w += wj * v[j].w;
+            }
+            M = mb;
         }
     }
     if (r >= p.gqa) return;
     const float inv = den > 0.f ? 1.f / den : 0.f;
-    T* op = static_cast<T*>(p.out) + orow * E;
-    for (int j = 0; j < nchunk; ++j) {
-        const int e = 4 * (sub + 8 * j);
-        store_quad<T>(op + e, acc[4 * j] * inv, acc[4 * j + 1] * inv, acc[4 * j + 2] * inv, acc[4 * j + 3] * inv);
-        if (p.out_f32)
-            *reinterpret_cast<float4*>(p.out_f32 + orow * E + e) =
-                make_float4(acc[4 * j] * inv, acc[4 * j + 1] * inv, acc[4 * j + 2] * inv, acc[4 * j + 3] * inv);
-    }
-    if (p.lse_out && sub == 0) p.lse_out[orow] = den > 0.f ? (lmax + __log2f(den)) * kLn2 : neg_inf();
+    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
+    store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, acc.x, acc.y, acc.z, acc.w);
+    if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = acc;
+    if (p.lse_out && c4 == 0) p.lse_out[orow] = den > 0.f ? (M + __log2f(den)) * kLn2 : neg_inf();
 }
 
 // ==================================================================================
@@ -1706,9 +1709,28 @@ int decode_validate(const dvattn_paged_args* a) {
     return DVATTN_OK;
 }
 
+// SM count x resident CTAs of a kernel on the current device, computed once per
+// (device, kernel) and cached: the attribute / occupancy queries cost microseconds of
+// host time per call otherwise.
 static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
+    struct Entry {
+        int dev;
+        const void* fn;
+        int n;
+    };
+    static Entry cache[256];
+    static int ncache = 0;
+    static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return DVATTN_ERR_CUDA;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        for (int i = 0; i < ncache; ++i)
+            if (cache[i].dev == dev && cache[i].fn == kc.fn) {
+                n_launch = cache[i].n;
+                return DVATTN_OK;
+            }
+    }
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return DVATTN_ERR_CUDA;
     if (cudaFuncSetAttribute(kc.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kc.smem) != cudaSuccess)
@@ -1717,6 +1739,8 @@ static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kc.fn, kc.nt, kc.smem) != cudaSuccess) return DVATTN_ERR_CUDA;
     if (occ < 1) occ = 1;
     n_launch = sms * occ;
+    std::lock_guard<std::mutex> lk(mu);
+    if (ncache < 256) cache[ncache++] = {dev, kc.fn, n_launch};
     return DVATTN_OK;
 }
 
@@ -1791,12 +1815,33 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         }
     }
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_MERGE) {
-        const unsigned segs = (unsigned)p.WS * (unsigned)p.Hkv;
+        const void* mk = nullptr;
         switch (dtype) {
-            case DVATTN_FLOAT16: decode_merge_kernel<__half><<<segs, 128, 0, stream>>>(p, p.E); break;
-            case DVATTN_BFLOAT16: decode_merge_kernel<__nv_bfloat16><<<segs, 128, 0, stream>>>(p, p.E); break;
-            default: decode_merge_kernel<float><<<segs, 128, 0, stream>>>(p, p.E); break;
+            case DVATTN_FLOAT16:
+                mk = p.E == 64 ? (const void*)&decode_merge_kernel<__half, 64>
+                   : p.E == 128 ? (const void*)&decode_merge_kernel<__half, 128> : (const void*)&decode_merge_kernel<__half, 256>;
+                break;
+            case DVATTN_BFLOAT16:
+                mk = p.E == 64 ? (const void*)&decode_merge_kernel<__nv_bfloat16, 64>
+                   : p.E == 128 ? (const void*)&decode_merge_kernel<__nv_bfloat16, 128>
+                                : (const void*)&decode_merge_kernel<__nv_bfloat16, 256>;
+                break;
+            default:
+                mk = p.E == 64 ? (const void*)&decode_merge_kernel<float, 64>
+                   : p.E == 128 ? (const void*)&decode_merge_kernel<float, 128> : (const void*)&decode_merge_kernel<float, 256>;
+                break;
         }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)p.WS * (unsigned)p.Hkv);
+        cfg.blockDim = dim3(16 * p.E / 4);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        void* margs[] = {&p};
+        if (cudaLaunchKernelExC(&cfg, mk, margs) != cudaSuccess) return DVATTN_ERR_CUDA;
     }
     return cudaGetLastError() == cudaSuccess ? DVATTN_OK : DVATTN_ERR_CUDA;
 }
