@@ -185,6 +185,8 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
     float* sLse = sML + WARPS * 16 * 2; // [16]
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    // programmatic dependent of the schedule kernel: wait for its header and prefix sums
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
@@ -499,6 +501,8 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    // programmatic dependent of the schedule kernel: wait for its header and prefix sums
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
@@ -869,6 +873,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     // smem [page chunk][head][panel][boxr rows][128 B].
     const int boxr_shift = __ffs(boxr) - 1;
     const uint32_t box_bytes = (uint32_t)Hkv * NPANEL * boxr * 128u;
+    // programmatic dependent of the schedule kernel: wait for its header and prefix sums
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
@@ -1267,6 +1273,8 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
     float* sP = sQ + 16 * LD;
 
     const int tid = threadIdx.x;
+    // programmatic dependent of the schedule kernel: wait for its header and prefix sums
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
@@ -1797,6 +1805,16 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
 
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) decode_prep_kernel<<<1, 1024, 0, stream>>>(p);
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_ATTEND) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(n_launch);
+        cfg.blockDim = dim3(kc.nt);
+        cfg.dynamicSmemBytes = kc.smem;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
         if (kc.tma) {
             alignas(64) CUtensorMap mk, mv;
             const int win = kc.row ? 16 * kc.cw / p.Hkv : 64;
@@ -1806,12 +1824,10 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
             if (!enc(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) || !enc(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
                 return DVATTN_ERR_CUDA;
             void* args[] = {&p, &mk, &mv, &boxr};
-            if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)
-                return DVATTN_ERR_CUDA;
+            if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;
         } else {
             void* args[] = {&p};
-            if (cudaLaunchKernel(kc.fn, dim3(n_launch), dim3(kc.nt), args, kc.smem, stream) != cudaSuccess)
-                return DVATTN_ERR_CUDA;
+            if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;
         }
     }
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_MERGE) {

@@ -99,6 +99,8 @@ __device__ __forceinline__ int cta_of(long long u, long long U, int n) {
 __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
     __shared__ long long warp_tot[32];
     __shared__ long long carry_s;
+    // let the attention kernel launch now; it waits (griddepcontrol.wait) for our results
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     if (tid == 0) carry_s = 0;
     __syncthreads();
