@@ -253,7 +253,36 @@ def run_reference(args, world, rank):
                              "sample": desc},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "gpu_launches": 0}
+    rc = reference_cuda_timing(name) if not args.no_ref_cuda else None
+    if rc:
+        line["reference_cuda_gpu"] = rc
     print(json.dumps(line), flush=True)
+
+
+def reference_cuda_timing(name):
+    """The reference's own CUDA op (its src/binding.cu built for sm_100a into oracle/_ref)
+    on the full workload, in a subprocess (it registers the same torch.ops.libdvatt
+    namespace), device-resident inputs, mean over 20 calls.  None when unavailable
+    (library not built, no GPU, or a shape its kernels reject: they need E = 128, GQA 16)."""
+    import subprocess
+    import tempfile
+    so = os.path.join(ROOT, "oracle", "_ref", "dvatt_ref.so")
+    if not os.path.exists(so) or not torch.cuda.is_available() or name not in ("config1", "config2", "config3"):
+        return None
+    from dvattn_b200 import workloads as wl
+    case = {"config1": wl.config1, "config2": wl.config2, "config3": wl.config3}[name]()
+    with tempfile.TemporaryDirectory() as d:
+        src, dst = os.path.join(d, "in.pt"), os.path.join(d, "out.pt")
+        torch.save(dict(kind="paged", args=case.op_args(None)[1:], out_shape=tuple(case.new_out().shape),
+                        dtype=case.dtype), src)
+        r = subprocess.run([sys.executable, os.path.join(ROOT, "oracle", "run_ref.py"), src, dst, "20"],
+                           capture_output=True, text=True, timeout=900)
+        if r.returncode != 0:
+            return {"unavailable": (r.stderr.strip().splitlines() or ["failed"])[-1][:200]}
+        us = torch.load(dst)["us"]
+    return {"value": round(wl.paged_bytes(case) / (us * 1e-6) / 1e9, 2), "unit": "GB/s",
+            "us_per_layer_step": round(us, 2),
+            "note": "reference's own CUDA op (oracle/_ref, built for sm_100a) on the same config, device inputs"}
 
 
 def run_ours(args, world, rank, local):
@@ -376,6 +405,57 @@ def run_ours(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_varlen(args, world, rank, local):
+    """Config 4 (bf16 varlen chunked prefill): tensor-bound; metric TFLOP/s of the attended
+    q.k and p.v products.  Weak scaling: every rank runs its own batch of 16 sequences."""
+    from dvattn_b200 import capi
+    from dvattn_b200 import workloads as wl
+    from oracle import dvattn_oracle as O  # CPU baseline leg only
+    dev = f"cuda:{local}"
+    _, tf_peak, peak_kind = load_peaks()
+    case = wl.config4(device=dev)
+    flops = wl.varlen_flops(case)
+    out = case.new_out()
+    call = capi.VarlenCall(*case.capi_args(out))
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    total = sum_over_ranks(float(flops), world)
+    value = total / (t_ms * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        tl, ql = wl.config4_lengths(4, 16)
+        cs = wl.make_varlen(tl[:1], ql[:1], Hq=32, Hkv=2, E=128, R=32, BS=16, dtype=torch.bfloat16, seed=4)
+        a = (cs.scale, cs.locations, cs.queries, cs.cosines, cs.sines, cs.fragment_lengths, cs.k_cache, cs.v_cache,
+             cs.block_tables, cs.cu_seqlens_q)
+        O.varlen_paged_sdpa_f32(*a)
+        t0 = time.perf_counter()
+        O.varlen_paged_sdpa_f32(*a)
+        dt = time.perf_counter() - t0
+        cpu = {"value": round(wl.varlen_flops(cs) / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+               "kind": "port", "sample": "first sequence of config 4"}
+    if rank == 0:
+        print(json.dumps({"metric": "varlen prefill attention TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s",
+                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 4),
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bfloat16",
+                          "data": "synthetic (seeded)", "config": {"workload": "config4: bf16 varlen prefill, 16 seqs, "
+                                                                                "32/2 heads, E=128, R=32, page 16"},
+                          "roofline": {"bound": "tensor", "achieved": round(flops / (t_ms * 1e-3) / 1e12, 3),
+                                       "peak": tf_peak, "peak_kind": peak_kind, "unit": "TFLOP/s",
+                                       "frac": round(flops / (t_ms * 1e-3) / 1e12 / tf_peak, 4), "traffic": None},
+                          "gpu_launches": 3 * args.steps, "cpu_baseline": cpu}), flush=True)
+
+
 def run_long3(args, world, rank, local):
     """Config 3 with its KV split across the ranks (page-aligned chunks) and the partial
     outputs merged over NCCL (all-gather of f32 O + LSE, then the LSE-merge kernel)."""
@@ -425,8 +505,9 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config1", "config2", "config3", "config5", "long3"])
+    ap.add_argument("--workload", default="config2", choices=["config1", "config2", "config3", "config4", "config5", "long3"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-ref-cuda", action="store_true", help="reference arm: skip timing the reference CUDA op")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -436,6 +517,8 @@ def main():
     world, rank, local = dist_setup(args.gpus)
     if args.workload == "long3":
         run_long3(args, world, rank, local)
+    elif args.workload == "config4":
+        run_varlen(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
     if world > 1:
