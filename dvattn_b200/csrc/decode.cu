@@ -17,6 +17,16 @@
 
 namespace dvb {
 
+// Scratch instrumentation: compiled only with -DDVB_TRACE (never in the product build).
+#ifdef DVB_TRACE
+__device__ unsigned long long g_trace[8][4096];
+#define DVB_TC(k) do { if (blockIdx.x < 4096) g_trace[k][blockIdx.x] = global_ns(); } while (0)
+#define DVB_TADD(k, v) do { if (blockIdx.x < 4096) atomicAdd(&g_trace[k][blockIdx.x], (unsigned long long)(v)); } while (0)
+#else
+#define DVB_TC(k) do { } while (0)
+#define DVB_TADD(k, v) do { } while (0)
+#endif
+
 // ----------------------------------------------------------------------------------
 // query rotation of one (row ws, KV head, turn f) into shared memory.
 // rotated[e] = q[e]*c[e] - q[e+R/2]*s[e]          for e < R/2
@@ -84,6 +94,9 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
             }
         }
         named_bar_sync(bar_id, nth);
+#ifdef DVB_TRACE
+        if (tid == 0) DVB_TADD(5, global_ns());
+#endif
 #pragma unroll
         for (int k = 0; k < MAXT; ++k) {
             const int t = tid + k * nth;
@@ -129,17 +142,72 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
     }
 }
 
+// In-place variant for the row kernel: cp.async copies every raw q chunk straight into
+// the swizzled slot its rotated value will occupy (rows g >= gqa are zero-filled), then
+// each thread rotates the pairs it owns -- both slots of a pair belong to one thread, so
+// the update is in place with no register staging.  The caller follows with a barrier.
+template <class T, int E>
+__device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, int f, int nh, uint8_t* sQ, int tid,
+                                                 int nth, float* sCS, int bar_id) {
+    constexpr int CH = E / 8;
+    const int w = ws / p.S, s = ws - w * p.S;
+    const float* cr = p.cos + ((size_t)f * p.WS + ws) * p.cs_stride;
+    const float* sr = p.sin + ((size_t)f * p.WS + ws) * p.cs_stride;
+    const int R = p.R, hp = R >> 1;
+    if (!((hp & 7) == 0 && ((reinterpret_cast<uintptr_t>(cr) | reinterpret_cast<uintptr_t>(sr)) & 15) == 0)) {
+        rotate_q_rows<T, E, 1>(p, ws, f, 0, nh, sQ, tid, nth, sCS, bar_id);  // general path (scalar)
+        return;
+    }
+    auto slot = [&](int row, int ch) -> uint8_t* {
+        return sQ + ((row >> 4) * (E / 64) + (ch >> 3)) * 2048 + (row & 15) * 128 + (((ch & 7) ^ (row & 7)) << 4);
+    };
+    for (int t = tid; t < nh * 16 * CH; t += nth) {
+        const int row = t / CH, ch = t - row * CH;
+        const int g = row & 15;
+        const T* q = static_cast<const T*>(p.q) +
+                     (((size_t)w * p.Hq + (row >> 4) * p.gqa + (g < p.gqa ? g : 0)) * p.S + s) * E + ch * 8;
+        cp_async16_zfill(smem_u32(slot(row, ch)), q, g < p.gqa ? 16 : 0);
+    }
+    for (int k = tid; k < 2 * (hp >> 2); k += nth) {
+        const int half = k / (hp >> 2), jj = k - half * (hp >> 2);
+        cp_async16_zfill(smem_u32(sCS + half * hp + jj * 4), (half ? sr : cr) + jj * 4, 16);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    named_bar_sync(bar_id, nth);
+    const int npair = hp >> 3;
+    for (int t = tid; t < nh * 16 * npair; t += nth) {
+        const int row = t / npair, j = t - row * npair;
+        uint4* xa = reinterpret_cast<uint4*>(slot(row, j));
+        uint4* ya = reinterpret_cast<uint4*>(slot(row, j + npair));
+        uint4 xv = *xa, yv = *ya;
+        const T* x = reinterpret_cast<const T*>(&xv);
+        const T* y = reinterpret_cast<const T*>(&yv);
+        uint32_t lo[4], hi[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const float c0 = sCS[j * 8 + 2 * u], c1 = sCS[j * 8 + 2 * u + 1];
+            const float s0 = sCS[hp + j * 8 + 2 * u], s1 = sCS[hp + j * 8 + 2 * u + 1];
+            const float x0 = Elem<T>::to_f(x[2 * u]), x1 = Elem<T>::to_f(x[2 * u + 1]);
+            const float y0 = Elem<T>::to_f(y[2 * u]), y1 = Elem<T>::to_f(y[2 * u + 1]);
+            lo[u] = Elem<T>::pack2(x0 * c0 - y0 * s0, x1 * c1 - y1 * s1);
+            hi[u] = Elem<T>::pack2(y0 * c0 + x0 * s0, y1 * c1 + x1 * s1);
+        }
+        *xa = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *ya = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    }
+}
+
 // L2 prefetch of what rotate_q_rows will read for (ws, f): the q rows of all heads and
 // the cos/sin rows (bulk prefetch wants 16-byte aligned, 16-byte multiple ranges).
 template <class T, int E>
 __device__ __forceinline__ void prefetch_rotation_inputs(const PagedParams& p, int ws, int f, int lane) {
     const int w = ws / p.S, s = ws - w * p.S;
     if (p.S == 1) {
-        if (lane == 0) {
-            const T* q = static_cast<const T*>(p.q) + (size_t)w * p.Hq * E;
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"((uint32_t)(p.Hq * E * sizeof(T)))
-                         : "memory");
-        }
+        // the row's q block (Hq * E elements, contiguous): one L2 prefetch per 128-B line
+        const char* q = reinterpret_cast<const char*>(static_cast<const T*>(p.q) + (size_t)w * p.Hq * E);
+        const int lines = (int)((p.Hq * E * sizeof(T) + 127) / 128);
+        for (int i = lane; i < lines; i += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(q + (size_t)i * 128));
     } else {
         for (int hq = lane; hq < p.Hq; hq += 32) {
             const T* q = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
@@ -190,7 +258,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
-    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    const long long u0 = p.cstart[c], u1 = p.cstart[c + 1];
     if (u0 >= u1) return;
     const int ws0 = find_row<NT>(p, u0);
 
@@ -506,7 +574,7 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
-    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    const long long u0 = p.cstart[c], u1 = p.cstart[c + 1];
     if (u0 >= u1) return;
     const int ws0 = find_row<C::NT>(p, u0);
 
@@ -867,6 +935,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    if (tid == 0) DVB_TC(0);
     const int Hkv = p.Hkv;
     const int TOKB = (CW / Hkv) * 16;           // keys per stage (window)
     // One TMA box = one page (or the window's part of it) for all heads and panels:
@@ -878,7 +947,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
-    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    const long long u0 = p.cstart[c], u1 = p.cstart[c + 1];
     if (u0 >= u1) return;
     const int ws0 = find_row<C::NT>(p, u0);
 
@@ -1002,27 +1071,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         return (uint32_t)((((row >> boxr_shift) * Hkv + h) * NPANEL + (ch >> 3)) * boxr + (row & (boxr - 1))) * 128u +
                (uint32_t)(((ch & 7) ^ (row & 7)) << 4);
     };
-    for (int i = 0;; ++i) {
-        if (named_bar_or(1, CW * 32, *sAbort != 0)) break;
-        const int st = i % STAGES;
-        if (!mbar_wait(bar_full + st * 8, (i / STAGES) & 1)) {
-            if (lane == 0) {
-                *sAbort = 1;
-                atomicOr(&p.sched->error, 2);
-            }
-            continue;
-        }
-        const StageDesc d = sDesc[st];
-        if (d.n < 0) break;
-        if (d.flags & 1) {
-            m0 = m1 = neg_inf();
-            l0 = l1 = 0.f;
-#pragma unroll
-            for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-        }
-        if (d.flags & 2) {
-            named_bar_sync(2, CW * 32);
-            rotate_q_rows<T, E, (CW * 16 * (E / 8) + CW * 32 - 1) / (CW * 32)>(p, d.ws, d.f, 0, Hkv, sQ, tid, CW * 32,
+    // The first tile always starts a turn: rotate its q now, while the first stage's TMA
+    // loads are in flight, instead of after they land.
+    {
+        TileIter<64> it0;
+        it0.init(p, ws0, u0, u1);
+        it0.align = TOKB;
+        TileDesc d0;
+        if (it0.next(p, d0)) {
+            rotate_q_inplace<T, E>(p, d0.ws, d0.f, Hkv, sQ, tid, CW * 32,
                                                                            reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
@@ -1033,6 +1090,50 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                             qf[kk][2], qf[kk][3]);
                 }
             }
+        }
+    }
+    for (int i = 0;; ++i) {
+        if (named_bar_or(1, CW * 32, *sAbort != 0)) break;
+        const int st = i % STAGES;
+        if (!mbar_wait(bar_full + st * 8, (i / STAGES) & 1)) {
+            if (lane == 0) {
+                *sAbort = 1;
+                atomicOr(&p.sched->error, 2);
+            }
+            continue;
+        }
+        if (tid == 0 && i == 0) DVB_TC(1);
+        const StageDesc d = sDesc[st];
+        if (d.n < 0) {
+            if (tid == 0) DVB_TC(2);
+            break;
+        }
+        if (d.flags & 1) {
+            m0 = m1 = neg_inf();
+            l0 = l1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        }
+        if ((d.flags & 2) && i > 0) {
+#ifdef DVB_TRACE
+            const unsigned long long tr0 = global_ns();
+            if (tid == 0) DVB_TADD(6, tr0);
+#endif
+            named_bar_sync(2, CW * 32);
+            rotate_q_inplace<T, E>(p, d.ws, d.f, Hkv, sQ, tid, CW * 32,
+                                                                           reinterpret_cast<float*>(smem + C::OFF_CS), 2);
+            named_bar_sync(2, CW * 32);
+            if constexpr (C::QREG) {
+#pragma unroll
+                for (int kk = 0; kk < C::KS; ++kk) {
+                    const int ch = kk * 2 + (lane >> 4), row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                    ldsm_x4(qh + (ch >> 3) * 2048 + row * 128 + (((ch & 7) ^ (row & 7)) << 4), qf[kk][0], qf[kk][1],
+                            qf[kk][2], qf[kk][3]);
+                }
+            }
+#ifdef DVB_TRACE
+            if (tid == 0) { DVB_TADD(3, global_ns() - tr0); DVB_TADD(4, 1); }
+#endif
         }
 
         const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
@@ -1278,7 +1379,7 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
     const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
     if (c >= sch.n_eff) return;
-    const long long u0 = cta_start(c, sch.U, sch.n_eff), u1 = cta_start(c + 1, sch.U, sch.n_eff);
+    const long long u0 = p.cstart[c], u1 = p.cstart[c + 1];
     if (u0 >= u1) return;
     const int ws0 = find_row<NT>(p, u0);
     const float* __restrict__ kc = static_cast<const float*>(p.k);
@@ -1485,12 +1586,12 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     }
     const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
     const int n = sch.n_eff;
-    const int ca = cta_of(b, sch.U, n), cb = cta_of(b + V - 1, sch.U, n);
+    const int ca = cta_of(p.cstart, b, n), cb = cta_of(p.cstart, b + V - 1, n);
     if (ca == cb) return;
     __shared__ int s_part[NTH];
     const int npc = cb - ca + 1;
     const int hh = p.slot_heads > 1 ? hkv : 0;
-    const bool ca_not_first = cta_start(ca, sch.U, n) < b;
+    const bool ca_not_first = p.cstart[ca] < b;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float M = neg_inf(), den = 0.f;
     for (int base = 0; base < npc; base += NTH) {
@@ -1499,7 +1600,8 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
         if (tid < cnt) {
             const int cc = ca + base + tid;
             const int slot = (cc == ca && ca_not_first) ? 2 * ca + 1 : 2 * cc;
-            s_part[tid] = (slot * p.slot_heads + hh) * 16;
+            // a CTA whose range is empty (boundaries snapped together) wrote no piece
+            s_part[tid] = p.cstart[cc] == p.cstart[cc + 1] ? -1 : (slot * p.slot_heads + hh) * 16;
         }
         __syncthreads();
         if (r >= p.gqa) continue;
@@ -1510,7 +1612,7 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
             for (int j = 0; j < B; ++j) {
                 l[j] = neg_inf();
                 v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k0 + j < cnt) {
+                if (k0 + j < cnt && s_part[k0 + j] >= 0) {
                     const int pi = s_part[k0 + j] + r;
                     l[j] = p.part_lse[pi];
                     v[j] = reinterpret_cast<const float4*>(p.part_o + (size_t)pi * E)[c4];
@@ -1753,14 +1855,15 @@ static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
 }
 
 struct DecodeLayout {
-    size_t off_P, off_rs, off_po, off_pl, total;
+    size_t off_P, off_rs, off_cs, off_po, off_pl, total;
 };
 static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int slot_heads) {
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
     DecodeLayout L;
     L.off_P = 256;
     L.off_rs = L.off_P + up(sizeof(long long) * (size_t)(WS + 1));
-    L.off_po = L.off_rs + (varlen ? up(sizeof(int) * (size_t)WS) : 0);
+    L.off_cs = L.off_rs + (varlen ? up(sizeof(int) * (size_t)WS) : 0);
+    L.off_po = L.off_cs + up(sizeof(long long) * (size_t)(n_launch + 1));
     L.off_pl = L.off_po + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16 * E);
     L.total = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16);
     return L;
@@ -1800,6 +1903,14 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.row_seq = p.cu_q ? reinterpret_cast<int*>(wsb + L.off_rs) : nullptr;
     p.part_o = reinterpret_cast<float*>(wsb + L.off_po);
     p.part_lse = reinterpret_cast<float*>(wsb + L.off_pl);
+    p.cstart = reinterpret_cast<long long*>(wsb + L.off_cs);
+    {
+        // a query rotation costs about as long as streaming ~96 KB of the cache
+        const int esz = dtype == DVATTN_FLOAT32 ? 4 : 2;
+        const long long unit_bytes = (long long)(kc.row ? p.Hkv : 1) * 2 * p.E * esz;
+        const long long ru = (96 * 1024) / unit_bytes;
+        p.rot_units = (int)(ru < 8 ? 8 : ru);
+    }
     p.n_launch = n_launch;
     p.min_units = kc.min_units;
 

@@ -62,6 +62,8 @@ struct PagedParams {
     int hsplit;
     int slot_heads;
     int bs_shift;      // log2(block_size) when it is a power of two, else -1
+    long long* cstart; // [n_launch + 1] first unit of each CTA's range (written by the prep kernel)
+    int rot_units;     // units charged for a turn start (its query rotation) in the balanced split
 };
 
 __device__ __forceinline__ int row_block_table(const PagedParams& p, int ws) {
@@ -76,29 +78,36 @@ __device__ __forceinline__ int turn_vis(int L, int loc, int off, int cap) {
     return v > 0 ? v : 0;
 }
 
+// Units of one row segment: each turn with visible keys counts its keys plus
+// rot_units for its query rotation, so the balanced split charges CTAs for the
+// rotations they do, not only for the keys they stream.
+__device__ __forceinline__ int turn_units(int vis, int rot) { return vis > 0 ? vis + rot : 0; }
 __device__ __forceinline__ int seg_visible(const PagedParams& p, int ws) {
     int off = 0, tot = 0;
     for (int f = 0; f < p.F; ++f) {
         int L = __ldg(p.L + f);
-        tot += turn_vis(L, __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap);
+        tot += turn_units(turn_vis(L, __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap), p.rot_units);
         off += L;
     }
     return tot;
 }
 
-__device__ __forceinline__ long long cta_start(long long c, long long U, int n) { return c * U / n; }
-
-// CTA whose unit range contains u (ranges are non-empty because U >= n).
-__device__ __forceinline__ int cta_of(long long u, long long U, int n) {
-    int c = (int)(u * n / U);
-    if (c + 1 < n && cta_start(c + 1, U, n) <= u) ++c;
-    return c;
+// CTA whose (non-empty) unit range contains u: the largest c < n with cstart[c] <= u.
+__device__ __forceinline__ int cta_of(const long long* cstart, long long u, int n) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (cstart[mid] <= u) lo = mid; else hi = mid - 1;
+    }
+    return lo;
 }
 
 // One pass over the schedule: fills P and the header.  Single CTA of 1024 threads.
 __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
     __shared__ long long warp_tot[32];
     __shared__ long long carry_s;
+    constexpr int kSharedRows = 2048;  // rows whose prefix sums are also kept in shared memory
+    __shared__ long long sP[kSharedRows + 1];
     // let the attention kernel launch now; it waits (griddepcontrol.wait) for our results
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -128,7 +137,10 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
         __syncthreads();
         const long long carry = carry_s;
         const long long excl = carry + (wid ? warp_tot[wid - 1] : 0) + x - v;
-        if (ws < p.WS) p.P[ws] = excl;
+        if (ws < p.WS) {
+            p.P[ws] = excl;
+            if (ws <= kSharedRows) sP[ws] = excl;
+        }
         __syncthreads();
         if (tid == 1023) carry_s = excl + v;
         __syncthreads();
@@ -145,15 +157,60 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
             p.row_seq[t] = lo < p.nseq ? lo : 0;
         }
     }
+    __shared__ int n_s;
+    __shared__ long long U_s;
     if (tid == 0) {
         const long long tot = carry_s;
         p.P[p.WS] = tot;
+        if (p.WS <= kSharedRows) sP[p.WS] = tot;
         const long long U = tot * p.hsplit;
         long long want = (U + p.min_units - 1) / p.min_units;
         int n = (int)(want < p.n_launch ? want : p.n_launch);
+        n = U > 0 ? (n > 0 ? n : 1) : 0;
         p.sched->U = U;
         p.sched->error = 0;
-        p.sched->n_eff = U > 0 ? (n > 0 ? n : 1) : 0;
+        p.sched->n_eff = n;
+        n_s = n;
+        U_s = U;
+    }
+    __syncthreads();
+    // CTA boundaries: c * U / n, moved back to the start of a turn when they fall inside
+    // the rotation units of that turn, so every turn's rotation is done by the CTA that
+    // streams the turn's first keys.
+    const int n = n_s;
+    const long long U = U_s;
+    const long long* Pq = p.WS <= kSharedRows ? sP : p.P;
+    for (int c = tid; c <= n; c += 1024) {
+        long long u = (n > 0) ? (long long)c * U / n : 0;
+        if (c > 0 && c < n) {
+            int lo = 0, hi = p.WS - 1;  // row: largest ws with P[ws] * hsplit <= u
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (Pq[mid] * p.hsplit <= u) lo = mid; else hi = mid - 1;
+            }
+            const int ws = lo;
+            const long long V = Pq[ws + 1] - Pq[ws];
+            if (V > 0) {
+                const long long r = u - Pq[ws] * p.hsplit;
+                long long acc = (r / V) * V;  // start of the segment (KV head) within the row
+                int off = 0;
+                for (int f = 0; f < p.F; ++f) {
+                    const int L = __ldg(p.L + f);
+                    const int tu = turn_units(turn_vis(L, __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap), p.rot_units);
+                    // (turn start, end of its rotation units]: snap to the turn start, so
+                    // a non-empty range holding a turn's rotation units also holds its
+                    // first key
+                    if (tu > 0 && r <= acc + p.rot_units) {
+                        u -= r - acc;
+                        break;
+                    }
+                    if (r < acc + tu) break;
+                    acc += tu;
+                    off += L;
+                }
+            }
+        }
+        p.cstart[c] = (c == n) ? U : u;
     }
 }
 
@@ -191,13 +248,13 @@ template <int TILE> struct TileIter {
         f = 0;
         off = 0;
         vis = turn_vis(__ldg(p.L), __ldg(p.loc + ws), 0, p.cap);
-        while (ts >= vis) {
-            ts -= vis;
+        while (ts >= turn_units(vis, p.rot_units)) {
+            ts -= turn_units(vis, p.rot_units);
             off += __ldg(p.L + f);
             ++f;
             vis = turn_vis(__ldg(p.L + f), __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap);
         }
-        t = ts;
+        t = ts - p.rot_units;  // negative while inside the turn's rotation units
         rem = u1 - u0;
         pend_seg = pend_turn = true;
         first_seg = true;
@@ -206,10 +263,18 @@ template <int TILE> struct TileIter {
 
     __device__ __forceinline__ bool next(const PagedParams& p, TileDesc& d) {
         if (rem <= 0) return false;
-        while (t >= vis) {
+        for (;;) {
+            if (t < 0) {  // rotation units: cost only, no keys
+                const int k = (long long)(-t) < rem ? -t : (int)rem;
+                t += k;
+                rem -= k;
+                seg_left -= k;
+                if (rem <= 0) return false;
+                continue;
+            }
+            if (t < vis) break;
             off += __ldg(p.L + f);
             ++f;
-            t = 0;
             pend_turn = true;
             if (f == p.F) {
                 f = 0;
@@ -224,6 +289,7 @@ template <int TILE> struct TileIter {
                 first_seg = false;
             }
             vis = turn_vis(__ldg(p.L + f), __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap);
+            t = vis > 0 ? -p.rot_units : 0;
         }
         int n = vis - t;
         if (n > TILE) n = TILE;
