@@ -9,6 +9,7 @@
 // dvattn_paged_attention_gpu (src/kernels/paged_kernel_v21.cuh:17-431).
 #include "decode.cuh"
 #include "schedule.cuh"
+#include "tma_host.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -1720,51 +1721,6 @@ bool pick_tma(int dtype, int E, KernelChoice& kc) {
     return false;
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    if (!fn) {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    }
-    return fn;
-}
-
-// [tokens = NB*BS][Hkv][E] cache as a 3-D map, box = 64 columns x 1 head x boxr tokens,
-// 128-byte swizzle.
-// [tokens][Hkv][E] cache as a 4-D map {64 columns, tokens, E/64 panels, Hkv heads} whose box
-// {64, boxr, E/64, Hkv} is one page for all heads, landing as [head][panel][row][128 B]
-// with the 128-byte swizzle.
-bool encode_cache_map_all_heads(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long tokens,
-                                int boxr) {
-    auto fn = tensor_map_encoder();
-    if (!fn) return false;
-    cuuint64_t dims[4] = {64, (cuuint64_t)tokens, (cuuint64_t)(E / 64), (cuuint64_t)Hkv};
-    cuuint64_t strides[3] = {(cuuint64_t)Hkv * E * 2, 128, (cuuint64_t)E * 2};
-    cuuint32_t box[4] = {64, (cuuint32_t)boxr, (cuuint32_t)(E / 64), (cuuint32_t)Hkv};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    const CUtensorMapDataType dt =
-        dtype == DVATTN_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    return fn(m, dt, 4, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-bool encode_cache_map(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long tokens, int boxr) {
-    auto fn = tensor_map_encoder();
-    if (!fn) return false;
-    cuuint64_t dims[3] = {(cuuint64_t)E, (cuuint64_t)Hkv, (cuuint64_t)tokens};
-    cuuint64_t strides[2] = {(cuuint64_t)E * 2, (cuuint64_t)Hkv * E * 2};
-    cuuint32_t box[3] = {64, 1, (cuuint32_t)boxr};
-    cuuint32_t es[3] = {1, 1, 1};
-    const CUtensorMapDataType dt =
-        dtype == DVATTN_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
 
 template <class T, int E>
 KernelChoice tc_choice() {
@@ -2020,6 +1976,7 @@ size_t varlen_workspace_size(const dvattn_varlen_args* v) {
     if (!v || v->W < 0 || v->T < 0) return 0;
     dvattn_paged_args a = varlen_as_paged(v);
     if (decode_validate(&a) != DVATTN_OK) return 0;
+    if (prefill_eligible(v)) return prefill_workspace_size(v);
     KernelChoice kc;
     choose(a.dtype, a.E, a.Hkv, a.block_size, a.num_blocks, kc);
     int n_launch = 0;
@@ -2040,6 +1997,7 @@ int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, c
     if (misaligned16(v->queries) || misaligned16(v->k_cache) || misaligned16(v->v_cache) || misaligned16(v->out) ||
         (v->out_f32 && misaligned16(v->out_f32)))
         return DVATTN_ERR_INVALID_ARGUMENT;
+    if (prefill_eligible(v)) return prefill_launch(v, workspace, wbytes, stream);
     PagedParams p{};
     p.F = v->F; p.W = v->T; p.Hq = v->Hq; p.Hkv = v->Hkv; p.E = v->E; p.S = 1; p.R = v->R;
     p.BS = v->block_size; p.maxb = v->max_blocks_per_seq; p.WS = v->T; p.gqa = v->Hq / v->Hkv;
