@@ -1,15 +1,22 @@
 // Varlen chunked prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// A CTA serves one work item: 8 consecutive packed query tokens of one sequence and one
-// KV head, i.e. M = 128 query rows (token j = row / 16, head g = row % 16).  It streams
-// that sequence's visible keys of every turn in 128-key windows:
-//   warp 0      producer: block-table lookups + 3-D TMA page boxes into a 2-stage ring
-//   warp 1      MMA issuer (one thread): S = Q K^T into TMEM (double-buffered), then
-//               O += P V into TMEM, completion signalled by tcgen05.commit on mbarriers
-//   warps 2..5  softmax: each thread owns one query row = one TMEM lane; it reads its S
-//               row, applies the row's causal bound, keeps the online max/sum, rescales
-//               its O row in TMEM when the max moves, writes P (bf16/f16) to shared
-//               memory for the PV MMA, and finally normalises and stores the output.
+// A CTA serves one work item: 2 x 128 packed query rows of one sequence and one KV head.
+// A row is (token j, head g of the KV group); with G = gqa rounded up to a power of two,
+// a 128-row tile holds 128 / G consecutive tokens (row = j * G + g), and the item holds
+// two such tiles, A and B.  It streams the sequence's visible keys of every turn in
+// 128-key windows:
+//   warp 8      producer: block-table lookups + 3-D TMA page boxes into a 2-stage ring
+//   warp 9      MMA issuer (one thread): S_A = Q_A K^T, S_B = Q_B K^T into TMEM, then
+//               O_A += P_A V, O_B += P_B V with P read from TMEM; completion is signalled
+//               by tcgen05.commit on mbarriers.  Issue order S_A(i), PV_B(i-1), S_B(i),
+//               PV_A(i) lets the tensor core work for one tile while the other's softmax
+//               runs (ping-pong).
+//   warps 0..3  softmax of tile A, warps 4..7 softmax of tile B: each thread owns one
+//               query row = one TMEM lane; it reads its S row, applies the row's causal
+//               bound, keeps the online max/sum (rescaling its O row in TMEM only when
+//               the max grows by more than 2^8, so the exponentials stay bounded), and
+//               writes P (bf16/f16) over its S row in TMEM for the PV MMA.  At the end it
+//               normalises its O row and stores the output row.
 // The query rotation of each turn is fused: each softmax thread copies its raw q row
 // (cp.async) into the swizzled A-operand tile and rotates it in place.
 //
@@ -25,21 +32,20 @@
 namespace dvb {
 namespace pf {
 
-constexpr int QT = 8;                  // query tokens per work item
-constexpr int M = 128;                 // query rows (QT x 16 heads)
+constexpr int M = 128;                 // query rows per tile (two tiles per item)
 constexpr int KT = 128;                // keys per window
 constexpr int E = 128;                 // head dim (E == Ev)
 constexpr int PANEL = 128 * 128;       // one 64-column panel of a 128-row tile (bytes)
 constexpr int TILE = 2 * PANEL;        // 128 rows x 128 columns, 16-bit
 constexpr int STAGES = 2;
-constexpr size_t OFF_Q = 0;
-constexpr size_t OFF_P = OFF_Q + TILE;
-constexpr size_t OFF_K = OFF_P + TILE;
+constexpr size_t OFF_Q = 0;                         // Q_A, Q_B
+constexpr size_t OFF_K = OFF_Q + 2 * TILE;
 constexpr size_t OFF_V = OFF_K + STAGES * TILE;
 constexpr size_t OFF_BAR = OFF_V + STAGES * TILE;  // 16 mbarriers
 constexpr size_t OFF_MISC = OFF_BAR + 16 * 8;      // tmem base, abort flag
 constexpr size_t SMEM = OFF_MISC + 64;
-constexpr int NT = 6 * 32;
+constexpr int NT = 10 * 32;
+constexpr int WARP_PRODUCER = 8, WARP_MMA = 9;
 
 struct Item {
     int w, t0, nt, hkv;
@@ -47,6 +53,8 @@ struct Item {
 
 struct Params {
     int F, T, W, Hq, Hkv, gqa, R, BS, maxb, cap;
+    int gshift;  // log2 of G, the rows per token in a tile (gqa rounded up to a power of 2)
+    int tpi;     // tokens per item = 2 * 128 / G
     long long NB;
     float scale_log2;
     void* out;
@@ -120,6 +128,32 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Registers written by tcgen05.ld hold their values only after tcgen05.wait::ld: this
+// empty volatile statement re-defines them after the wait so no use moves above it.
+template <int N> __device__ __forceinline__ void reg_fence(float* v) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+// A operand from TMEM (P), B from shared memory (V).
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        : "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ int turn_vis_pf(int L, int loc, int off, int cap) {
     int v = min(L, loc + 1);
@@ -131,7 +165,7 @@ __device__ __forceinline__ int turn_vis_pf(int L, int loc, int off, int cap) {
 // Token t belongs to the first sequence w with t < cu_q[w+1], else to sequence 0
 // (varlen_paged_kernel_v21.cuh:40-47).  With a non-decreasing cu_q that gives W + 1
 // contiguous segments: segment w = [w ? cu[w] : 0, cu[w+1]) of sequence w, and segment W
-// = [cu[W], T) of sequence 0.  Each segment is cut into 8-token tiles x Hkv items; the
+// = [cu[W], T) of sequence 0.  Each segment is cut into tpi-token pieces x Hkv items; the
 // items are laid out segment by segment in decreasing order of the segment's key count
 // (its last token's visible keys over all turns), the last tile of a segment first, so
 // the longest work starts first.
@@ -180,22 +214,33 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(Params p) {
         for (int r = 0; r < NS; ++r) {
             const int s = rank[r];
             start[s] = acc;
-            acc += (sb[s] - sa[s] + QT - 1) / QT * p.Hkv;
+            acc += (sb[s] - sa[s] + p.tpi - 1) / p.tpi * p.Hkv;
         }
         p.header[0] = acc < p.max_items ? acc : p.max_items;
         p.header[1] = 0;
     }
     __syncthreads();
     for (int s = tid; s < NS; s += 1024) {
-        const int a = sa[s], b = sb[s], ntile = (b - a + QT - 1) / QT;
+        const int a = sa[s], b = sb[s], ntile = (b - a + p.tpi - 1) / p.tpi;
         int k = start[s];
         for (int q = ntile - 1; q >= 0; --q)
             for (int h = 0; h < p.Hkv; ++h, ++k)
-                if (k < p.max_items) p.items[k] = Item{s < p.W ? s : 0, a + q * QT, min(QT, b - a - q * QT), h};
+                if (k < p.max_items) p.items[k] = Item{s < p.W ? s : 0, a + q * p.tpi, min(p.tpi, b - a - q * p.tpi), h};
     }
 }
 
 // ---- the prefill kernel ---------------------------------------------------------
+// Keys the item's tokens can see in turn f (the union of their visible ranges), by a
+// whole warp: lanes split the tokens, then a max-reduction.
+__device__ __forceinline__ int item_span(const Params& p, const Item& it, int f, int off, int lane) {
+    const int L = __ldg(p.L + f);
+    int v = 0;
+    for (int j = lane; j < it.nt; j += 32) v = max(v, turn_vis_pf(L, __ldg(p.loc + (size_t)f * p.T + it.t0 + j), off, p.cap));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
 template <class T>
 __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_constant__ CUtensorMap tmk,
                                                         const __grid_constant__ CUtensorMap tmv) {
@@ -210,27 +255,26 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     const Item it = p.items[blockIdx.x];
     const bool bf16 = Elem<T>::dtype == DVATTN_BFLOAT16;
 
+    // mbarriers: [0,2) kv_full, [2,4) kv_empty, [4,6) s_full, [6,8) p_full, [8,10) q_ready, 10 o_done
     const uint32_t bar = s0 + (uint32_t)OFF_BAR;
-    const uint32_t kv_full = bar, kv_empty = bar + 16, s_full = bar + 32, s_free = bar + 48;
-    const uint32_t p_full = bar + 64, o_done = bar + 72, q_ready = bar + 80, fin = bar + 88;
+    const uint32_t kv_full = bar, kv_empty = bar + 16, s_full = bar + 32, p_full = bar + 48, q_ready = bar + 64;
+    const uint32_t o_done = bar + 80;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
 
     if (tid == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < 2; ++s) {
             mbar_init(kv_full + 8 * s, 1);
             mbar_init(kv_empty + 8 * s, 1);
             mbar_init(s_full + 8 * s, 1);
-            mbar_init(s_free + 8 * s, 4);
+            mbar_init(p_full + 8 * s, 128);
+            mbar_init(q_ready + 8 * s, 128);
         }
-        mbar_init(p_full, 128);
         mbar_init(o_done, 1);
-        mbar_init(q_ready, 128);
-        mbar_init(fin, 1);
         *sAbort = 0;
         fence_mbar_init();
     }
-    if (wid == 1) {  // TMEM: S0 [0,128), S1 [128,256), O [256,384)
+    if (wid == WARP_MMA) {  // TMEM columns: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(s0 + (uint32_t)OFF_MISC)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -240,16 +284,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    // per-turn window plan, identical in every role: the union of the tokens' visible
-    // ranges, in 128-aligned windows of logical positions
-    auto turn_span = [&](int f, int off) {
-        int vmax = 0;
-        for (int j = 0; j < it.nt; ++j)
-            vmax = max(vmax, turn_vis_pf(p.L[f], p.loc[(size_t)f * p.T + it.t0 + j], off, p.cap));
-        return vmax;
-    };
-
-    if (wid == 0) {
+    if (wid == WARP_PRODUCER) {
         // =============================== producer ===============================
         if (lane == 0) {
             prefetch_tmap(&tmk);
@@ -257,275 +292,287 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         }
         const int* btw = p.bt + (size_t)it.w * p.maxb;
         const int pages = KT / p.BS;
-        const uint32_t bytes = 2u * TILE;
         int i = 0, off = 0;
         bool ok = true;
         for (int f = 0; f < p.F && ok; ++f) {
-            const int L = p.L[f];
-            const int vmax = turn_span(f, off);
-            if (vmax > 0) {
-                for (int win = off & ~(KT - 1); win < off + vmax && ok; win += KT, ++i) {
-                    const int st = i & 1;
-                    if (*sAbort || (i >= STAGES && !mbar_wait(kv_empty + 8 * st, ((i >> 1) - 1) & 1))) {
-                        ok = false;
-                        break;
-                    }
-                    if (lane == 0) mbar_expect_tx(kv_full + 8 * st, bytes);
-                    __syncwarp();
-                    for (int j = lane; j < pages; j += 32) {
-                        const int pos = win + j * p.BS;  // first logical position of page j
-                        const bool need = pos + p.BS > off && pos < off + vmax && (pos / p.BS) < p.maxb;
-                        int page = need ? __ldg(btw + pos / p.BS) : -1;
-                        const bool valid = need && (p.NB <= 0 || (page >= 0 && page < p.NB));
-                        const int z = valid ? page * p.BS : -2 * p.BS;  // out of bounds -> zeros
-                        const uint32_t dk = s0 + (uint32_t)(OFF_K + st * TILE + j * p.BS * 128);
-                        const uint32_t dv = s0 + (uint32_t)(OFF_V + st * TILE + j * p.BS * 128);
+            const int vmax = item_span(p, it, f, off, lane);
+            for (int win = off & ~(KT - 1); vmax > 0 && win < off + vmax; win += KT, ++i) {
+                const int st = i & 1;
+                if (*sAbort || (i >= STAGES && !mbar_wait(kv_empty + 8 * st, ((i >> 1) - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) mbar_expect_tx(kv_full + 8 * st, 2u * TILE);
+                __syncwarp();
+                for (int j = lane; j < pages; j += 32) {
+                    const int pos = win + j * p.BS;  // first logical position of page j
+                    const bool need = pos + p.BS > off && pos < off + vmax && (pos / p.BS) < p.maxb;
+                    const int page = need ? __ldg(btw + pos / p.BS) : -1;
+                    const bool valid = need && page >= 0 && page < p.NB;
+                    const int z = valid ? page * p.BS : -2 * p.BS;  // out of bounds -> zeros
+                    const uint32_t dk = s0 + (uint32_t)(OFF_K + st * TILE + j * p.BS * 128);
+                    const uint32_t dv = s0 + (uint32_t)(OFF_V + st * TILE + j * p.BS * 128);
 #pragma unroll
-                        for (int pn = 0; pn < 2; ++pn) {
-                            tma_load_3d(dk + pn * PANEL, &tmk, pn * 64, it.hkv, z, kv_full + 8 * st);
-                            tma_load_3d(dv + pn * PANEL, &tmv, pn * 64, it.hkv, z, kv_full + 8 * st);
-                        }
+                    for (int pn = 0; pn < 2; ++pn) {
+                        tma_load_3d(dk + pn * PANEL, &tmk, pn * 64, it.hkv, z, kv_full + 8 * st);
+                        tma_load_3d(dv + pn * PANEL, &tmv, pn * 64, it.hkv, z, kv_full + 8 * st);
                     }
                 }
             }
-            off += L;
+            off += __ldg(p.L + f);
         }
         if (!ok && lane == 0) {
             *sAbort = 1;
             atomicOr(p.header + 1, 1);
         }
-    } else if (wid == 1) {
+    } else if (wid == WARP_MMA) {
         // ================================ MMA ================================
         const uint32_t id_s = idesc(bf16, M, KT, false);
         const uint32_t id_o = idesc(bf16, M, E, true);
-        int i = 0, off = 0, turn = 0;
-        bool ok = true, any = false;
-        int pend = -1;  // tile whose PV is still to be issued
-        auto issue_pv = [&](int tile) {
-            if (!mbar_wait(p_full, tile & 1)) return false;
-            tc_fence_after();
+        // S_grp = Q_grp K^T over the 128 head dims (8 k-steps of 16)
+        auto issue_s = [&](int grp, int st) {
             if (lane == 0) {
-                const int st = tile & 1;
 #pragma unroll
-                for (int kk = 0; kk < KT / 16; ++kk) {
-                    const uint64_t a = sdesc(s0 + (uint32_t)(OFF_P + (kk >> 2) * PANEL + (kk & 3) * 32), 16, 1024);
-                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_V + st * TILE + kk * 16 * 128), PANEL, 1024);
-                    umma(tmem + 256, a, b, id_o, (tile > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < E / 16; ++kk) {
+                    const uint32_t ko = (uint32_t)((kk >> 2) * PANEL + (kk & 3) * 32);
+                    const uint64_t a = sdesc(s0 + (uint32_t)(OFF_Q + grp * TILE) + ko, 16, 1024);
+                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_K + st * TILE) + ko, 16, 1024);
+                    umma(tmem + 128 * grp, a, b, id_s, kk > 0 ? 1u : 0u);
                 }
-                umma_commit(o_done);
-                umma_commit(kv_empty + 8 * st);
+                umma_commit(s_full + 8 * grp);
             }
             __syncwarp();
-            return true;
         };
-        for (int f = 0; f < p.F && ok; ++f) {
-            const int vmax = turn_span(f, off);
-            if (vmax > 0) {
-                if (!mbar_wait(q_ready, turn & 1)) { ok = false; break; }
-                ++turn;
-                for (int win = off & ~(KT - 1); win < off + vmax; win += KT, ++i) {
-                    const int st = i & 1;
-                    if (!mbar_wait(kv_full + 8 * st, (i >> 1) & 1)) { ok = false; break; }
-                    if (i >= 2 && !mbar_wait(s_free + 8 * st, ((i >> 1) - 1) & 1)) { ok = false; break; }
-                    tc_fence_after();
-                    if (lane == 0) {
+        // O_grp += P_grp V over the 128 keys; P is packed 2 per column over S_grp's columns
+        auto issue_pv = [&](int grp, int st, bool acc) {
+            if (lane == 0) {
 #pragma unroll
-                        for (int kk = 0; kk < E / 16; ++kk) {
-                            const uint64_t a = sdesc(s0 + (uint32_t)(OFF_Q + (kk >> 2) * PANEL + (kk & 3) * 32), 16, 1024);
-                            const uint64_t b =
-                                sdesc(s0 + (uint32_t)(OFF_K + st * TILE + (kk >> 2) * PANEL + (kk & 3) * 32), 16, 1024);
-                            umma(tmem + 128 * st, a, b, id_s, kk > 0 ? 1u : 0u);
-                        }
-                        umma_commit(s_full + 8 * st);
-                    }
-                    __syncwarp();
-                    any = true;
-                    if (pend >= 0 && !issue_pv(pend)) { ok = false; break; }
-                    pend = i;
+                for (int kk = 0; kk < KT / 16; ++kk) {
+                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_V + st * TILE + kk * 16 * 128), PANEL, 1024);
+                    umma_ts(tmem + 256 + 128 * grp, tmem + 128 * grp + 8 * kk, b, id_o, (acc || kk > 0) ? 1u : 0u);
                 }
             }
-            off += p.L[f];
+            __syncwarp();
+        };
+        int i = 0, off = 0, turn = 0, prev_st = 0;
+        bool ok = true;
+        for (int f = 0; f < p.F && ok; ++f) {
+            const int vmax = item_span(p, it, f, off, lane);
+            for (int win = off & ~(KT - 1); vmax > 0 && win < off + vmax; win += KT, ++i) {
+                const int st = i & 1;
+                const bool first = win == (off & ~(KT - 1));
+                if (!mbar_wait(kv_full + 8 * st, (i >> 1) & 1)) { ok = false; break; }
+                if (first && !mbar_wait(q_ready, turn & 1)) { ok = false; break; }
+                tc_fence_after();
+                issue_s(0, st);
+                if (i > 0) {
+                    if (!mbar_wait(p_full + 8, (i - 1) & 1)) { ok = false; break; }
+                    tc_fence_after();
+                    issue_pv(1, prev_st, i - 1 > 0);
+                    if (lane == 0) umma_commit(kv_empty + 8 * prev_st);
+                    __syncwarp();
+                }
+                if (first && !mbar_wait(q_ready + 8, turn & 1)) { ok = false; break; }
+                tc_fence_after();
+                issue_s(1, st);
+                if (!mbar_wait(p_full, i & 1)) { ok = false; break; }
+                tc_fence_after();
+                issue_pv(0, st, i > 0);
+                prev_st = st;
+            }
+            if (vmax > 0) ++turn;
+            off += __ldg(p.L + f);
         }
-        if (ok && pend >= 0 && !issue_pv(pend)) ok = false;
+        if (ok && i > 0) {
+            if (mbar_wait(p_full + 8, (i - 1) & 1)) {
+                tc_fence_after();
+                issue_pv(1, prev_st, i - 1 > 0);
+            } else {
+                ok = false;
+            }
+        }
         if (!ok && lane == 0) {
             *sAbort = 1;
             atomicOr(p.header + 1, 2);
         }
-        (void)any;
-        // all MMAs issued by this thread have completed before TMEM is released
-        if (lane == 0) umma_commit(fin);
+        // o_done: every MMA of the item has completed (the epilogue and the TMEM release
+        // wait on it)
+        if (lane == 0) umma_commit(o_done);
         __syncwarp();
-        mbar_wait(fin, 0);
+        mbar_wait(o_done, 0);
     } else {
         // ============================== softmax ==============================
+        const int grp = wid >> 2;                 // tile A (0) or B (1)
         const int r = (wid & 3) * 32 + lane;     // query row == TMEM lane
         const uint32_t lane_base = (uint32_t)((wid & 3) * 32) << 16;
-        const int j = r >> 4, g = r & 15;        // token, head within the KV group
-        const bool row_ok = j < it.nt && g < p.gqa;
-        const int t = it.t0 + j;
-        const int hq = it.hkv * p.gqa + g;
+        const uint32_t tS = tmem + lane_base + 128 * grp;
+        const uint32_t tO = tmem + lane_base + 256 + 128 * grp;
+        const int tok = (grp << (7 - p.gshift)) + (r >> p.gshift);  // token index within the item
+        const int g = r & ((1 << p.gshift) - 1);
+        const bool row_ok = tok < it.nt && g < p.gqa;
+        const int t = it.t0 + (row_ok ? tok : 0);
+        const int hq = it.hkv * p.gqa + (row_ok ? g : 0);
         const float sl2 = p.scale_log2;
-        float m = neg_inf(), l = 0.f;
+        const uint32_t qtile = (uint32_t)(OFF_Q + grp * TILE);
+        float m = neg_inf(), l = 0.f;  // running max (log2 units, stepped) and sum
         int i = 0, off = 0;
         bool ok = true;
         const int hp = p.R >> 1;
         for (int f = 0; f < p.F && ok; ++f) {
-            const int L = p.L[f];
-            const int vmax = turn_span(f, off);
+            const int L = __ldg(p.L + f);
+            const int vmax = item_span(p, it, f, off, lane);
             if (vmax > 0) {
                 // ---- rotate this row's q for turn f into the A tile (in place) ----
-                {
-                    const T* qrow = static_cast<const T*>(p.q) + ((size_t)(row_ok ? t : 0) * p.Hq + (row_ok ? hq : 0)) * E;
-                    for (int ch = 0; ch < E / 8; ++ch)
-                        cp_async16_zfill(s0 + (uint32_t)(OFF_Q + (ch >> 3) * PANEL + r * 128 + (((ch & 7) ^ (r & 7)) << 4)),
-                                         qrow + ch * 8, row_ok ? 16 : 0);
-                    cp_async_commit();
-                    cp_async_wait<0>();
-                    if (row_ok) {
-                        const float* cr = p.cos + ((size_t)f * p.T + t) * hp;
-                        const float* sr = p.sin + ((size_t)f * p.T + t) * hp;
-                        for (int c = 0; c < hp / 8; ++c) {
-                            uint4* xa = reinterpret_cast<uint4*>(smem + OFF_Q + (c >> 3) * PANEL + r * 128 +
-                                                                 (((c & 7) ^ (r & 7)) << 4));
-                            const int c2 = c + hp / 8;
-                            uint4* ya = reinterpret_cast<uint4*>(smem + OFF_Q + (c2 >> 3) * PANEL + r * 128 +
-                                                                 (((c2 & 7) ^ (r & 7)) << 4));
-                            uint4 xv = *xa, yv = *ya;
-                            const T* x = reinterpret_cast<const T*>(&xv);
-                            const T* y = reinterpret_cast<const T*>(&yv);
-                            uint32_t lo[4], hi[4];
+                const T* qrow = static_cast<const T*>(p.q) + ((size_t)t * p.Hq + hq) * E;
 #pragma unroll
-                            for (int u = 0; u < 4; ++u) {
-                                const float c0 = cr[c * 8 + 2 * u], c1 = cr[c * 8 + 2 * u + 1];
-                                const float z0 = sr[c * 8 + 2 * u], z1 = sr[c * 8 + 2 * u + 1];
-                                const float x0 = Elem<T>::to_f(x[2 * u]), x1 = Elem<T>::to_f(x[2 * u + 1]);
-                                const float y0 = Elem<T>::to_f(y[2 * u]), y1 = Elem<T>::to_f(y[2 * u + 1]);
-                                lo[u] = Elem<T>::pack2(x0 * c0 - y0 * z0, x1 * c1 - y1 * z1);
-                                hi[u] = Elem<T>::pack2(y0 * c0 + x0 * z0, y1 * c1 + x1 * z1);
-                            }
-                            *xa = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                            *ya = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                for (int ch = 0; ch < E / 8; ++ch)
+                    cp_async16_zfill(s0 + qtile + (uint32_t)((ch >> 3) * PANEL + r * 128 + (((ch & 7) ^ (r & 7)) << 4)),
+                                     qrow + ch * 8, row_ok ? 16 : 0);
+                cp_async_commit();
+                cp_async_wait<0>();
+                if (row_ok) {
+                    const float* cr = p.cos + ((size_t)f * p.T + t) * hp;
+                    const float* sr = p.sin + ((size_t)f * p.T + t) * hp;
+                    for (int c = 0; c < hp / 8; ++c) {
+                        const int c2 = c + hp / 8;
+                        uint4* xa = reinterpret_cast<uint4*>(smem + qtile + (c >> 3) * PANEL + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+                        uint4* ya = reinterpret_cast<uint4*>(smem + qtile + (c2 >> 3) * PANEL + r * 128 + (((c2 & 7) ^ (r & 7)) << 4));
+                        uint4 xv = *xa, yv = *ya;
+                        const T* x = reinterpret_cast<const T*>(&xv);
+                        const T* y = reinterpret_cast<const T*>(&yv);
+                        uint32_t lo[4], hi[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const float c0 = __ldg(cr + c * 8 + 2 * u), c1 = __ldg(cr + c * 8 + 2 * u + 1);
+                            const float z0 = __ldg(sr + c * 8 + 2 * u), z1 = __ldg(sr + c * 8 + 2 * u + 1);
+                            const float x0 = Elem<T>::to_f(x[2 * u]), x1 = Elem<T>::to_f(x[2 * u + 1]);
+                            const float y0 = Elem<T>::to_f(y[2 * u]), y1 = Elem<T>::to_f(y[2 * u + 1]);
+                            lo[u] = Elem<T>::pack2(x0 * c0 - y0 * z0, x1 * c1 - y1 * z1);
+                            hi[u] = Elem<T>::pack2(y0 * c0 + x0 * z0, y1 * c1 + x1 * z1);
                         }
+                        *xa = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *ya = make_uint4(hi[0], hi[1], hi[2], hi[3]);
                     }
-                    fence_proxy_async_smem();
-                    mbar_arrive(q_ready);
                 }
-                // this row's last visible logical position in turn f (-1: none)
-                const int lim = row_ok ? off + turn_vis_pf(L, p.loc[(size_t)f * p.T + t], off, p.cap) - 1 : -1;
-                const int vend = off + vmax;  // keys of this turn past the union's end are zeroed in V
+                fence_proxy_async_smem();
+                mbar_arrive(q_ready + 8 * grp);
+                // visible window of this row in turn f: logical positions [off, lim]
+                const int lim = row_ok ? off + turn_vis_pf(L, __ldg(p.loc + (size_t)f * p.T + t), off, p.cap) - 1 : off - 1;
+                const int vend = off + vmax;
                 for (int win = off & ~(KT - 1); win < off + vmax; win += KT, ++i) {
                     const int st = i & 1;
-                    if (!mbar_wait(s_full + 8 * st, (i >> 1) & 1)) { ok = false; break; }
+                    if (!mbar_wait(s_full + 8 * grp, i & 1)) { ok = false; break; }
                     tc_fence_after();
                     float sv[KT];
 #pragma unroll
-                    for (int c = 0; c < KT / 32; ++c) tmem_ld32(tmem + lane_base + 128 * st + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
+                    for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
                     tmem_wait_ld();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(s_free + 8 * st);
-                    // mask: logical position win + c visible iff off <= pos <= lim
-                    float mx = neg_inf();
+                    reg_fence<KT>(sv);
+                    const int lo = off - win, hi = lim - win;  // visible columns [lo, hi]
+                    if (!__all_sync(0xffffffffu, lo <= 0 && hi >= KT - 1)) {
 #pragma unroll
-                    for (int c = 0; c < KT; ++c) {
-                        const int pos = win + c;
-                        const float x = (pos >= off && pos <= lim) ? sv[c] * sl2 : neg_inf();
-                        sv[c] = x;
-                        mx = fmaxf(mx, x);
+                        for (int c = 0; c < KT; ++c)
+                            if (c < lo || c > hi) sv[c] = neg_inf();
                     }
-                    const float mn = fmaxf(m, mx);
-                    const float mu = mn == neg_inf() ? 0.f : mn;
-                    const float alpha = fast_exp2(m - mu);
-                    float ps = 0.f;
+                    float mx[8];
 #pragma unroll
-                    for (int c = 0; c < KT; ++c) {
-                        sv[c] = fast_exp2(sv[c] - mu);
-                        ps += sv[c];
+                    for (int u = 0; u < 8; ++u) mx[u] = sv[u];
+#pragma unroll
+                    for (int c = 8; c < KT; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+                    const float mxs = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                            fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+                    // the reference point moves only when the max grows by more than 8
+                    // (a factor 256 in the exponentials); the result is exact either way
+                    const float mnew = mxs > m + 8.f ? mxs : m;
+                    const float alpha = mnew == m ? 1.f : ex2(m - mnew);
+                    const float mu = mnew == neg_inf() ? 0.f : mnew;
+                    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int c = 0; c < KT / 32; ++c) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) {
+                            const float e0 = ex2(fmaf(sv[32 * c + 2 * u], sl2, -mu));
+                            const float e1 = ex2(fmaf(sv[32 * c + 2 * u + 1], sl2, -mu));
+                            ps[u & 3] += e0 + e1;
+                            pk[u] = Elem<T>::pack2(e0, e1);
+                        }
+                        tmem_st16(tS + 16 * c, pk);
                     }
-                    l = l * alpha + ps;
-                    m = mn;
-                    // PV of the previous window must be done before O and P are touched
-                    if (i > 0) {
-                        if (!mbar_wait(o_done, (i - 1) & 1)) { ok = false; break; }
-                        tc_fence_after();
-                        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+                    l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+                    m = mnew;
+                    if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+                        // O holds the PV of every earlier window (their MMAs completed
+                        // before S of this window was signalled)
 #pragma unroll 1
-                            for (int c = 0; c < E / 32; ++c) {
-                                float ov[32];
-                                tmem_ld32(tmem + lane_base + 256 + 32 * c, ov);
-                                tmem_wait_ld();
+                        for (int c = 0; c < E / 32; ++c) {
+                            float ov[32];
+                            tmem_ld32(tO + 32 * c, ov);
+                            tmem_wait_ld();
+                            reg_fence<32>(ov);
 #pragma unroll
-                                for (int u = 0; u < 32; ++u) ov[u] *= alpha;
-                                tmem_st32(tmem + lane_base + 256 + 32 * c, ov);
-                            }
-                            tmem_wait_st();
+                            for (int u = 0; u < 32; ++u) ov[u] *= alpha;
+                            tmem_st32(tO + 32 * c, ov);
                         }
                     }
-                    // P row -> A tile of the PV MMA (keys along K, 128-byte swizzle)
-#pragma unroll
-                    for (int ch = 0; ch < KT / 8; ++ch) {
-                        uint4 pk;
-                        pk.x = Elem<T>::pack2(sv[8 * ch + 0], sv[8 * ch + 1]);
-                        pk.y = Elem<T>::pack2(sv[8 * ch + 2], sv[8 * ch + 3]);
-                        pk.z = Elem<T>::pack2(sv[8 * ch + 4], sv[8 * ch + 5]);
-                        pk.w = Elem<T>::pack2(sv[8 * ch + 6], sv[8 * ch + 7]);
-                        *reinterpret_cast<uint4*>(smem + OFF_P + (ch >> 3) * PANEL + r * 128 + (((ch & 7) ^ (r & 7)) << 4)) = pk;
-                    }
-                    // V rows of this window outside [off, vend) may hold another turn's or
-                    // uninitialised pool data: zero them (P is 0 there, but 0 * NaN is NaN)
-                    {
-                        const int pos = win + r;  // this thread's key row of the window
+                    if (grp == 0) {
+                        // V rows of this window outside [off, vend) may hold another turn's
+                        // or uninitialised pool data: zero them (P is 0 there, 0 * NaN is NaN)
+                        const int pos = win + r;
                         if (pos < off || pos >= vend) {
                             uint8_t* vrow = smem + OFF_V + st * TILE + r * 128;
+#pragma unroll
                             for (int c = 0; c < 8; ++c) {
                                 *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0u, 0u, 0u, 0u);
                                 *reinterpret_cast<uint4*>(vrow + PANEL + c * 16) = make_uint4(0u, 0u, 0u, 0u);
                             }
                         }
+                        fence_proxy_async_smem();
                     }
-                    fence_proxy_async_smem();
+                    tmem_wait_st();
                     tc_fence_before();
-                    mbar_arrive(p_full);
+                    mbar_arrive(p_full + 8 * grp);
                 }
             }
             off += L;
         }
-        if (!ok) {
-            if (lane == 0) {
-                *sAbort = 1;
-                atomicOr(p.header + 1, 8);
-            }
-        } else if (i > 0) {
-            // ---- epilogue: O / l -> output ----
-            if (mbar_wait(o_done, (i - 1) & 1)) {
-                tc_fence_after();
-                const float inv = l > 0.f ? 1.f / l : 0.f;
-                T* op = static_cast<T*>(p.out) + ((size_t)t * p.Hq + hq) * E;
+        if (!ok && lane == 0) {
+            *sAbort = 1;
+            atomicOr(p.header + 1, 8);
+        }
+        // ---- epilogue: O / l -> output ----
+        const bool done = mbar_wait(o_done, 0);
+        tc_fence_after();
+        if (ok && done && i > 0) {
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            T* op = static_cast<T*>(p.out) + ((size_t)t * p.Hq + hq) * E;
+            float* o32 = p.out_f32 ? p.out_f32 + ((size_t)t * p.Hq + hq) * E : nullptr;
 #pragma unroll 1
-                for (int c = 0; c < E / 32; ++c) {
-                    float ov[32];
-                    tmem_ld32(tmem + lane_base + 256 + 32 * c, ov);
-                    tmem_wait_ld();
-                    if (row_ok) {
+            for (int c = 0; c < E / 32; ++c) {
+                float ov[32];
+                tmem_ld32(tO + 32 * c, ov);
+                tmem_wait_ld();
+                reg_fence<32>(ov);
+                if (row_ok) {
 #pragma unroll
-                        for (int u = 0; u < 32; u += 8) {
-                            uint4 pk;
-                            pk.x = Elem<T>::pack2(ov[u] * inv, ov[u + 1] * inv);
-                            pk.y = Elem<T>::pack2(ov[u + 2] * inv, ov[u + 3] * inv);
-                            pk.z = Elem<T>::pack2(ov[u + 4] * inv, ov[u + 5] * inv);
-                            pk.w = Elem<T>::pack2(ov[u + 6] * inv, ov[u + 7] * inv);
-                            *reinterpret_cast<uint4*>(op + 32 * c + u) = pk;
-                            if (p.out_f32) {
-                                float* o32 = p.out_f32 + ((size_t)t * p.Hq + hq) * E + 32 * c + u;
-                                *reinterpret_cast<float4*>(o32) = make_float4(ov[u] * inv, ov[u + 1] * inv, ov[u + 2] * inv, ov[u + 3] * inv);
-                                *reinterpret_cast<float4*>(o32 + 4) =
-                                    make_float4(ov[u + 4] * inv, ov[u + 5] * inv, ov[u + 6] * inv, ov[u + 7] * inv);
-                            }
+                    for (int u = 0; u < 32; ++u) ov[u] *= inv;
+#pragma unroll
+                    for (int u = 0; u < 32; u += 8) {
+                        uint4 pk;
+                        pk.x = Elem<T>::pack2(ov[u], ov[u + 1]);
+                        pk.y = Elem<T>::pack2(ov[u + 2], ov[u + 3]);
+                        pk.z = Elem<T>::pack2(ov[u + 4], ov[u + 5]);
+                        pk.w = Elem<T>::pack2(ov[u + 6], ov[u + 7]);
+                        *reinterpret_cast<uint4*>(op + 32 * c + u) = pk;
+                        if (o32) {
+                            *reinterpret_cast<float4*>(o32 + 32 * c + u) = make_float4(ov[u], ov[u + 1], ov[u + 2], ov[u + 3]);
+                            *reinterpret_cast<float4*>(o32 + 32 * c + u + 4) =
+                                make_float4(ov[u + 4], ov[u + 5], ov[u + 6], ov[u + 7]);
                         }
                     }
                 }
-                if (row_ok && p.lse_out) p.lse_out[(size_t)t * p.Hq + hq] = l > 0.f ? (m + __log2f(l)) * kLn2 : neg_inf();
             }
+            if (row_ok && p.lse_out) p.lse_out[(size_t)t * p.Hq + hq] = l > 0.f ? (m + __log2f(l)) * kLn2 : neg_inf();
         }
         if (row_ok && i == 0) {  // no visible key at all: zeros
             T* op = static_cast<T*>(p.out) + ((size_t)t * p.Hq + hq) * E;
@@ -539,13 +586,21 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (wid == 1)
+    if (wid == WARP_MMA)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
 }  // namespace pf
 
 // ---------------------------------------------------------------------------------
+static int prefill_gshift(const dvattn_varlen_args* v) {
+    const int gqa = v->Hq / v->Hkv;
+    int s = 0;
+    while ((1 << s) < gqa) ++s;
+    return s;
+}
+static int prefill_tokens_per_item(const dvattn_varlen_args* v) { return 2 * (pf::M >> prefill_gshift(v)); }
+
 // DVATTN_PREFILL=0 keeps every varlen call on the split-KV decode schedule; =1 uses the
 // tensor-core prefill for every shape it supports, however small; unset: large calls only.
 static int prefill_mode() {
@@ -557,16 +612,18 @@ bool prefill_eligible(const dvattn_varlen_args* v) {
     const int mode = prefill_mode();
     if (mode == 0) return false;
     if (!v || (v->dtype != DVATTN_FLOAT16 && v->dtype != DVATTN_BFLOAT16)) return false;
-    if (v->E != 128 || v->Ev != 128 || v->Hkv <= 0 || v->Hq % v->Hkv || v->Hq / v->Hkv > 16) return false;
+    if (v->E != 128 || v->Ev != 128 || v->Hkv <= 0 || v->Hq < v->Hkv || v->Hq % v->Hkv || v->Hq / v->Hkv > 16) return false;
     if (v->R % 16 || v->R > v->E) return false;
     const int BS = v->block_size;
     if (!(BS == 8 || BS == 16 || BS == 32 || BS == 64 || BS == 128)) return false;
     if (v->num_blocks <= 0 || v->num_blocks * (long long)BS > 0x7fffffffLL) return false;
-    // enough 8-token tiles to fill the GPU; short prefills go through the decode schedule
-    return mode == 1 || (long long)(v->T / pf::QT) * v->Hkv >= 2 * 148;
+    // enough items to fill the GPU; short prefills go through the split-KV decode schedule
+    return mode == 1 || (long long)v->T * v->Hkv >= 148LL * prefill_tokens_per_item(v);
 }
 
-static int prefill_max_items(const dvattn_varlen_args* v) { return (v->T / pf::QT + v->W + 1) * v->Hkv; }
+static int prefill_max_items(const dvattn_varlen_args* v) {
+    return (v->T / prefill_tokens_per_item(v) + v->W + 1) * v->Hkv;
+}
 
 size_t prefill_workspace_size(const dvattn_varlen_args* v) {
     return 256 + sizeof(pf::Item) * (size_t)prefill_max_items(v);
@@ -577,6 +634,7 @@ int prefill_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, 
     if (!workspace || wbytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) return DVATTN_ERR_WORKSPACE;
     pf::Params p{};
     p.F = v->F; p.T = v->T; p.W = v->W; p.Hq = v->Hq; p.Hkv = v->Hkv; p.gqa = v->Hq / v->Hkv; p.R = v->R;
+    p.gshift = prefill_gshift(v); p.tpi = prefill_tokens_per_item(v);
     p.BS = v->block_size; p.maxb = v->max_blocks_per_seq;
     const long long cap = (long long)v->max_blocks_per_seq * v->block_size;
     p.cap = cap > 0x7fffffffLL ? 0x7fffffff : (int)cap;
