@@ -70,7 +70,8 @@ def traffic_from_profiles(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms; only the samples taken
+    between begin() and end() (the timed region) are summarised."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -80,11 +81,13 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.t0 = None
+        self.t1 = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -93,7 +96,13 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def begin(self):
+        self.t0 = time.time()
+
+    def end(self):
+        self.t1 = time.time()
 
     def stop(self):
         if self.proc is None:
@@ -105,7 +114,11 @@ class ClockSampler:
             self.proc.kill()
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        t0 = (self.t0 or 0.0) - 0.025
+        t1 = (self.t1 or time.time()) + 0.025
+        for ts, ln in self.lines:
+            if not t0 <= ts <= t1:
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -319,6 +332,8 @@ def run_ours(args, world, rank, local):
         time.sleep(0.3)
     barrier(world)
     torch.cuda.synchronize()
+    if sampler:
+        sampler.begin()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for i in range(args.steps):
@@ -338,6 +353,8 @@ def run_ours(args, world, rank, local):
         kev[i][1].record(stream)
         c.phase(capi.DVATTN_PHASE_MERGE)
     torch.cuda.synchronize()
+    if sampler:
+        sampler.end()
     clocks = sampler.stop() if sampler else None
     k_ms = statistics.mean(a.elapsed_time(b) for a, b in kev)
     k_ms = max_over_ranks(k_ms, world)
@@ -407,7 +424,12 @@ def run_ours(args, world, rank, local):
 
 def run_varlen(args, world, rank, local):
     """Config 4 (bf16 varlen chunked prefill): tensor-bound; metric TFLOP/s of the attended
-    q.k and p.v products.  Weak scaling: every rank runs its own batch of 16 sequences."""
+    q.k and p.v products (4 * E flops per visible (query head, key) pair).  Weak scaling:
+    every rank runs its own batch of 16 sequences.  Same legs as run_ours: value over the
+    C ABI with resident inputs (three rotating KV pools), the attention kernel alone between
+    events (phase ATTEND), e2e through torch.ops.libdvatt.dvattn_varlen_paged_sdpa with the
+    step's inputs copied from pinned host memory and the output copied back."""
+    import dvattn_b200  # registers torch.ops.libdvatt
     from dvattn_b200 import capi
     from dvattn_b200 import workloads as wl
     from oracle import dvattn_oracle as O  # CPU baseline leg only
@@ -416,20 +438,81 @@ def run_varlen(args, world, rank, local):
     case = wl.config4(device=dev)
     flops = wl.varlen_flops(case)
     out = case.new_out()
-    call = capi.VarlenCall(*case.capi_args(out))
-    for _ in range(args.warmup):
-        call()
+    pools = [(case.k_cache, case.v_cache)]
+    for _ in range(2):
+        pools.append((torch.randn_like(case.k_cache, dtype=torch.float32).to(case.dtype),
+                      torch.randn_like(case.v_cache, dtype=torch.float32).to(case.dtype)))
+    calls, ws = [], None
+    for kc, vc in pools:
+        a = list(case.capi_args(out))
+        a[7], a[8] = kc, vc
+        call = capi.VarlenCall(*a, workspace=ws)
+        ws = call.workspace
+        calls.append(call)
+    stream = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        calls[i % 3]()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.begin()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        calls[i % 3]()
+    e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        call()
-    e1.record()
-    torch.cuda.synchronize()
     t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps):
+        c = calls[i % 3]
+        c.phase(capi.DVATTN_PHASE_SCHEDULE)
+        kev[i][0].record(stream)
+        c.phase(capi.DVATTN_PHASE_ATTEND)
+        kev[i][1].record(stream)
+        c.phase(capi.DVATTN_PHASE_MERGE)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.end()
+    clocks = sampler.stop() if sampler else None
+    k_ms = max_over_ranks(statistics.mean(x.elapsed_time(y) for x, y in kev), world)
+
+    host_in = [t.cpu().pin_memory() for t in (case.queries, case.cosines, case.sines, case.locations,
+                                              case.fragment_lengths, case.block_tables, case.cu_seqlens_q)]
+    dev_in = [torch.empty_like(t, device=dev) for t in host_in]
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step(i):
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        q, cs, sn, loc, L, bt, cu = dev_in
+        kc, vc = pools[i % 3]
+        torch.ops.libdvatt.dvattn_varlen_paged_sdpa(out, case.scale, loc, q, cs, sn, L, kc, vc, bt, cu, cu)
+        host_out.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+
     total = sum_over_ranks(float(flops), world)
     value = total / (t_ms * 1e-3) / 1e12
+    e2e_val = total / (e2e_ms * 1e-3) / 1e12
+    achieved = flops / (k_ms * 1e-3) / 1e12
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         threads = len(os.sched_getaffinity(0))
@@ -445,15 +528,26 @@ def run_varlen(args, world, rank, local):
         cpu = {"value": round(wl.varlen_flops(cs) / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
                "kind": "port", "sample": "first sequence of config 4"}
     if rank == 0:
-        print(json.dumps({"metric": "varlen prefill attention TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s",
-                          "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 4),
-                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bfloat16",
-                          "data": "synthetic (seeded)", "config": {"workload": "config4: bf16 varlen prefill, 16 seqs, "
-                                                                                "32/2 heads, E=128, R=32, page 16"},
-                          "roofline": {"bound": "tensor", "achieved": round(flops / (t_ms * 1e-3) / 1e12, 3),
-                                       "peak": tf_peak, "peak_kind": peak_kind, "unit": "TFLOP/s",
-                                       "frac": round(flops / (t_ms * 1e-3) / 1e12 / tf_peak, 4), "traffic": None},
-                          "gpu_launches": 3 * args.steps, "cpu_baseline": cpu}), flush=True)
+        ks = "prefill_kernel" if case.queries.size(0) * case.k_cache.size(2) >= 148 * 16 else "decode_row_kernel"
+        print(json.dumps({
+            "metric": "varlen prefill attention TFLOP/s", "value": round(value, 3), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bfloat16",
+            "data": "synthetic (seeded N(0,1) q/k/v, seeded lengths and page permutation)",
+            "config": {"workload": "config4: bf16 varlen chunked prefill, 16 seqs, q ~ U[1,2048] after U[0,16384] "
+                                   "cached keys, 32/2 heads, E=128, R=32, page 16",
+                       "flops_per_step_per_gpu": flops, "parallelism": f"batch-replica x{world}",
+                       "l2": "3 rotating KV pools of %.0f MB each" %
+                             ((case.k_cache.numel() + case.v_cache.numel()) * case.k_cache.element_size() / 1e6)},
+            "roofline": {"bound": "tensor", "kernel": ks, "achieved": round(achieved, 3), "peak": tf_peak,
+                         "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4),
+                         "kernel_us": round(k_ms * 1e3, 2), "traffic": traffic_from_profiles("config4")},
+            "e2e": {"value": round(e2e_val, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_ms * 1e3, 2),
+                    "api": "torch.ops.libdvatt.dvattn_varlen_paged_sdpa"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu}), flush=True)
 
 
 def run_long3(args, world, rank, local):

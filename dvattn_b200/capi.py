@@ -40,6 +40,7 @@ EXPORTS = [
     "dvattn_paged_sdpa_workspace_size",
     "dvattn_paged_sdpa",
     "dvattn_paged_sdpa_phase",
+    "dvattn_varlen_paged_sdpa_phase",
     "dvattn_paged_sdpa_noalloc_max_workspace",
     "dvattn_paged_sdpa_noalloc",
     "dvattn_varlen_paged_sdpa_workspace_size",
@@ -89,6 +90,8 @@ def lib() -> ctypes.CDLL:
         L.dvattn_paged_sdpa.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _vp]
         L.dvattn_paged_sdpa_phase.restype = _i
         L.dvattn_paged_sdpa_phase.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _i, _vp]
+        L.dvattn_varlen_paged_sdpa_phase.restype = _i
+        L.dvattn_varlen_paged_sdpa_phase.argtypes = [ctypes.POINTER(VarlenArgs), _vp, ctypes.c_size_t, _i, _vp]
         L.dvattn_paged_sdpa_noalloc_max_workspace.restype = ctypes.c_size_t
         L.dvattn_paged_sdpa_noalloc_max_workspace.argtypes = []
         L.dvattn_paged_sdpa_noalloc.restype = _i
@@ -210,6 +213,12 @@ class VarlenCall:
                                             self.workspace.numel(), _stream(stream))
         if st != DVATTN_OK:
             raise DvattnError(st, "dvattn_varlen_paged_sdpa")
+
+    def phase(self, phase: int, stream: Optional[torch.cuda.Stream] = None) -> None:
+        st = lib().dvattn_varlen_paged_sdpa_phase(ctypes.byref(self.args), self.workspace.data_ptr(),
+                                                  self.workspace.numel(), phase, _stream(stream))
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_varlen_paged_sdpa_phase")
 
 
 def paged_sdpa(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,

@@ -32,7 +32,12 @@ size_t dvattn_varlen_paged_sdpa_workspace_size(const dvattn_varlen_args* args) {
 
 int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace, size_t workspace_bytes,
                              dvattn_stream_t stream) {
-    return dvb::varlen_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+    return dvb::varlen_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), DVATTN_PHASE_ALL);
+}
+
+int dvattn_varlen_paged_sdpa_phase(const dvattn_varlen_args* args, void* workspace, size_t workspace_bytes, int phase,
+                                   dvattn_stream_t stream) {
+    return dvb::varlen_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), phase);
 }
 
 int dvattn_rope(int dtype, int F, int W, int Hq, int S, int E, int R, void* out, const void* queries,

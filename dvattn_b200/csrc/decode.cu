@@ -1984,7 +1984,7 @@ size_t varlen_workspace_size(const dvattn_varlen_args* v) {
     return decode_layout(v->T, v->E, n_launch, true, kc.row ? v->Hkv : 1).total;
 }
 
-int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, cudaStream_t stream) {
+int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
     if (!v || v->W < 0 || v->T < 0) return DVATTN_ERR_INVALID_ARGUMENT;
     dvattn_paged_args a = varlen_as_paged(v);
     int st = decode_validate(&a);
@@ -1997,7 +1997,8 @@ int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, c
     if (misaligned16(v->queries) || misaligned16(v->k_cache) || misaligned16(v->v_cache) || misaligned16(v->out) ||
         (v->out_f32 && misaligned16(v->out_f32)))
         return DVATTN_ERR_INVALID_ARGUMENT;
-    if (prefill_eligible(v)) return prefill_launch(v, workspace, wbytes, stream);
+    if (phase < DVATTN_PHASE_ALL || phase > DVATTN_PHASE_MERGE) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (prefill_eligible(v)) return prefill_launch(v, workspace, wbytes, stream, phase);
     PagedParams p{};
     p.F = v->F; p.W = v->T; p.Hq = v->Hq; p.Hkv = v->Hkv; p.E = v->E; p.S = 1; p.R = v->R;
     p.BS = v->block_size; p.maxb = v->max_blocks_per_seq; p.WS = v->T; p.gqa = v->Hq / v->Hkv;
@@ -2009,7 +2010,7 @@ int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, c
     p.L = v->fragment_lengths; p.k = v->k_cache; p.v = v->v_cache; p.bt = v->block_tables;
     p.lse_out = v->lse_out; p.out_f32 = v->out_f32;
     p.cu_q = v->cu_seqlens_q; p.nseq = v->W; p.cs_stride = v->R / 2;
-    return run_schedule(p, v->dtype, workspace, wbytes, stream, DVATTN_PHASE_ALL);
+    return run_schedule(p, v->dtype, workspace, wbytes, stream, phase);
 }
 
 }  // namespace dvb

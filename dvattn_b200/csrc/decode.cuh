@@ -11,11 +11,11 @@ size_t decode_workspace_size(const dvattn_paged_args* a);
 int decode_launch(const dvattn_paged_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
 
 size_t varlen_workspace_size(const dvattn_varlen_args* a);
-int varlen_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream);
+int varlen_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
 // tcgen05 varlen prefill (prefill.cu): used by varlen_launch when prefill_eligible()
 bool prefill_eligible(const dvattn_varlen_args* a);
 size_t prefill_workspace_size(const dvattn_varlen_args* a);
-int prefill_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream);
+int prefill_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
 
 int rope_launch(int dtype, int F, int W, int Hq, int S, int E, int R, void* out, const void* q, const float* cos,
                 const float* sin, cudaStream_t stream);

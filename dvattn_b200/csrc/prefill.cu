@@ -37,12 +37,13 @@ constexpr int KT = 128;                // keys per window
 constexpr int E = 128;                 // head dim (E == Ev)
 constexpr int PANEL = 128 * 128;       // one 64-column panel of a 128-row tile (bytes)
 constexpr int TILE = 2 * PANEL;        // 128 rows x 128 columns, 16-bit
-constexpr int STAGES = 2;
+constexpr int KSTAGES = 3;             // K ring (freed after S = Q K^T)
+constexpr int VSTAGES = 2;             // V ring (freed after O += P V)
 constexpr size_t OFF_Q = 0;                         // Q_A, Q_B
 constexpr size_t OFF_K = OFF_Q + 2 * TILE;
-constexpr size_t OFF_V = OFF_K + STAGES * TILE;
-constexpr size_t OFF_BAR = OFF_V + STAGES * TILE;  // 16 mbarriers
-constexpr size_t OFF_MISC = OFF_BAR + 16 * 8;      // tmem base, abort flag
+constexpr size_t OFF_V = OFF_K + KSTAGES * TILE;
+constexpr size_t OFF_BAR = OFF_V + VSTAGES * TILE;  // 24 mbarrier slots
+constexpr size_t OFF_MISC = OFF_BAR + 24 * 8;       // tmem base, abort flag
 constexpr size_t SMEM = OFF_MISC + 64;
 constexpr int NT = 10 * 32;
 constexpr int WARP_PRODUCER = 8, WARP_MMA = 9;
@@ -229,6 +230,26 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(Params p) {
     }
 }
 
+// Scratch instrumentation: compiled only with -DPF_TRACE (never in the product build).
+#ifdef PF_TRACE
+__device__ unsigned long long g_pf_trace[256 * 16];
+#define PF_TR(i, slot) \
+    do { \
+        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (i) < 256) g_pf_trace[(i) * 16 + (slot)] = clock64(); \
+    } while (0)
+}  // namespace pf
+}  // namespace dvb
+extern "C" void dvb_pf_trace_read(unsigned long long* h) {
+    cudaMemcpyFromSymbol(h, dvb::pf::g_pf_trace, sizeof(dvb::pf::g_pf_trace));
+}
+namespace dvb {
+namespace pf {
+#else
+#define PF_TR(i, slot) \
+    do { \
+    } while (0)
+#endif
+
 // ---- the prefill kernel ---------------------------------------------------------
 // Keys the item's tokens can see in turn f (the union of their visible ranges), by a
 // whole warp: lanes split the tokens, then a max-reduction.
@@ -240,6 +261,44 @@ __device__ __forceinline__ int item_span(const Params& p, const Item& it, int f,
     for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
     return v;
 }
+
+// The item's sequence of 128-key windows: turn by turn, the windows covering the union
+// of the visible ranges.  Every role walks the same sequence (warp-wide calls).
+struct TileSeq {
+    int f, off, vmax, win;
+    int base, nwin, k;
+    bool valid;
+    __device__ __forceinline__ void seek(const Params& p, const Item& it, int lane) {
+        for (; f < p.F; ++f) {
+            vmax = item_span(p, it, f, off, lane);
+            if (vmax > 0) {
+                base = off & ~(KT - 1);
+                nwin = (off + vmax - base + KT - 1) / KT;
+                k = 0;
+                win = base;
+                valid = true;
+                return;
+            }
+            off += __ldg(p.L + f);
+        }
+        valid = false;
+    }
+    __device__ __forceinline__ void init(const Params& p, const Item& it, int lane) {
+        f = 0;
+        off = 0;
+        seek(p, it, lane);
+    }
+    __device__ __forceinline__ void next(const Params& p, const Item& it, int lane) {
+        if (++k < nwin) {
+            win += KT;
+            return;
+        }
+        off += __ldg(p.L + f);
+        ++f;
+        seek(p, it, lane);
+    }
+    __device__ __forceinline__ bool first() const { return k == 0; }
+};
 
 template <class T>
 __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_constant__ CUtensorMap tmk,
@@ -255,17 +314,22 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     const Item it = p.items[blockIdx.x];
     const bool bf16 = Elem<T>::dtype == DVATTN_BFLOAT16;
 
-    // mbarriers: [0,2) kv_full, [2,4) kv_empty, [4,6) s_full, [6,8) p_full, [8,10) q_ready, 10 o_done
+    // mbarriers: k_full[3], k_empty[3], v_full[2], v_empty[2], s_full[2], p_full[2],
+    // q_ready[2], o_done
     const uint32_t bar = s0 + (uint32_t)OFF_BAR;
-    const uint32_t kv_full = bar, kv_empty = bar + 16, s_full = bar + 32, p_full = bar + 48, q_ready = bar + 64;
-    const uint32_t o_done = bar + 80;
+    const uint32_t k_full = bar, k_empty = bar + 24, v_full = bar + 48, v_empty = bar + 64;
+    const uint32_t s_full = bar + 80, p_full = bar + 96, q_ready = bar + 112, o_done = bar + 128;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(smem + OFF_MISC);
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
 
     if (tid == 0) {
+        for (int s = 0; s < KSTAGES; ++s) {
+            mbar_init(k_full + 8 * s, 1);
+            mbar_init(k_empty + 8 * s, 1);
+        }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(kv_full + 8 * s, 1);
-            mbar_init(kv_empty + 8 * s, 1);
+            mbar_init(v_full + 8 * s, 1);
+            mbar_init(v_empty + 8 * s, 1);
             mbar_init(s_full + 8 * s, 1);
             mbar_init(p_full + 8 * s, 128);
             mbar_init(q_ready + 8 * s, 128);
@@ -292,34 +356,51 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         }
         const int* btw = p.bt + (size_t)it.w * p.maxb;
         const int pages = KT / p.BS;
-        int i = 0, off = 0;
+        // one 128-key window of K or V: a 3-D box {64 columns, 1 head, BS rows} per page
+        // and 64-column panel; pages outside the window's needed range, outside the block
+        // table or the pool load as zeros (out-of-bounds coordinate)
+        auto load = [&](const TileSeq& q, const CUtensorMap* map, uint32_t dst, uint32_t fullbar) {
+            if (lane == 0) mbar_expect_tx(fullbar, (uint32_t)TILE);
+            __syncwarp();
+            for (int j = lane; j < pages; j += 32) {
+                const int pos = q.win + j * p.BS;  // first logical position of page j
+                const bool need = pos + p.BS > q.off && pos < q.off + q.vmax && (pos / p.BS) < p.maxb;
+                const int page = need ? __ldg(btw + pos / p.BS) : -1;
+                const bool valid = need && page >= 0 && page < p.NB;
+                const int z = valid ? page * p.BS : -2 * p.BS;
+                const uint32_t d = dst + (uint32_t)(j * p.BS * 128);
+                tma_load_3d(d, map, 0, it.hkv, z, fullbar);
+                tma_load_3d(d + PANEL, map, 64, it.hkv, z, fullbar);
+            }
+        };
+        // K runs one window ahead of V: K(i+1) frees (S of window i-2 done) before V(i)
+        // does (PV of window i-2 done)
+        TileSeq kq, vq;
+        kq.init(p, it, lane);
+        vq.init(p, it, lane);
+        int ik = 0, iv = 0;
         bool ok = true;
-        for (int f = 0; f < p.F && ok; ++f) {
-            const int vmax = item_span(p, it, f, off, lane);
-            for (int win = off & ~(KT - 1); vmax > 0 && win < off + vmax; win += KT, ++i) {
-                const int st = i & 1;
-                if (*sAbort || (i >= STAGES && !mbar_wait(kv_empty + 8 * st, ((i >> 1) - 1) & 1))) {
+        while (vq.valid) {
+            while (kq.valid && ik <= iv + 1) {
+                const int ks = ik % KSTAGES;
+                if (*sAbort || (ik >= KSTAGES && !mbar_wait(k_empty + 8 * ks, (ik / KSTAGES - 1) & 1))) {
                     ok = false;
                     break;
                 }
-                if (lane == 0) mbar_expect_tx(kv_full + 8 * st, 2u * TILE);
-                __syncwarp();
-                for (int j = lane; j < pages; j += 32) {
-                    const int pos = win + j * p.BS;  // first logical position of page j
-                    const bool need = pos + p.BS > off && pos < off + vmax && (pos / p.BS) < p.maxb;
-                    const int page = need ? __ldg(btw + pos / p.BS) : -1;
-                    const bool valid = need && page >= 0 && page < p.NB;
-                    const int z = valid ? page * p.BS : -2 * p.BS;  // out of bounds -> zeros
-                    const uint32_t dk = s0 + (uint32_t)(OFF_K + st * TILE + j * p.BS * 128);
-                    const uint32_t dv = s0 + (uint32_t)(OFF_V + st * TILE + j * p.BS * 128);
-#pragma unroll
-                    for (int pn = 0; pn < 2; ++pn) {
-                        tma_load_3d(dk + pn * PANEL, &tmk, pn * 64, it.hkv, z, kv_full + 8 * st);
-                        tma_load_3d(dv + pn * PANEL, &tmv, pn * 64, it.hkv, z, kv_full + 8 * st);
-                    }
-                }
+                PF_TR(ik, 0);
+                load(kq, &tmk, s0 + (uint32_t)(OFF_K + ks * TILE), k_full + 8 * ks);
+                kq.next(p, it, lane);
+                ++ik;
             }
-            off += __ldg(p.L + f);
+            if (!ok) break;
+            const int vs = iv & 1;
+            if (*sAbort || (iv >= VSTAGES && !mbar_wait(v_empty + 8 * vs, ((iv >> 1) - 1) & 1))) {
+                ok = false;
+                break;
+            }
+            load(vq, &tmv, s0 + (uint32_t)(OFF_V + vs * TILE), v_full + 8 * vs);
+            vq.next(p, it, lane);
+            ++iv;
         }
         if (!ok && lane == 0) {
             *sAbort = 1;
@@ -330,13 +411,13 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         const uint32_t id_s = idesc(bf16, M, KT, false);
         const uint32_t id_o = idesc(bf16, M, E, true);
         // S_grp = Q_grp K^T over the 128 head dims (8 k-steps of 16)
-        auto issue_s = [&](int grp, int st) {
+        auto issue_s = [&](int grp, int ks) {
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < E / 16; ++kk) {
                     const uint32_t ko = (uint32_t)((kk >> 2) * PANEL + (kk & 3) * 32);
                     const uint64_t a = sdesc(s0 + (uint32_t)(OFF_Q + grp * TILE) + ko, 16, 1024);
-                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_K + st * TILE) + ko, 16, 1024);
+                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_K + ks * TILE) + ko, 16, 1024);
                     umma(tmem + 128 * grp, a, b, id_s, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(s_full + 8 * grp);
@@ -344,49 +425,54 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             __syncwarp();
         };
         // O_grp += P_grp V over the 128 keys; P is packed 2 per column over S_grp's columns
-        auto issue_pv = [&](int grp, int st, bool acc) {
+        auto issue_pv = [&](int grp, int vs, bool acc) {
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < KT / 16; ++kk) {
-                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_V + st * TILE + kk * 16 * 128), PANEL, 1024);
+                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_V + vs * TILE + kk * 16 * 128), PANEL, 1024);
                     umma_ts(tmem + 256 + 128 * grp, tmem + 128 * grp + 8 * kk, b, id_o, (acc || kk > 0) ? 1u : 0u);
                 }
             }
             __syncwarp();
         };
-        int i = 0, off = 0, turn = 0, prev_st = 0;
+        auto commit = [&](uint32_t b) {
+            if (lane == 0) umma_commit(b);
+            __syncwarp();
+        };
+        TileSeq ts;
+        ts.init(p, it, lane);
+        int i = 0, turn = 0;
         bool ok = true;
-        for (int f = 0; f < p.F && ok; ++f) {
-            const int vmax = item_span(p, it, f, off, lane);
-            for (int win = off & ~(KT - 1); vmax > 0 && win < off + vmax; win += KT, ++i) {
-                const int st = i & 1;
-                const bool first = win == (off & ~(KT - 1));
-                if (!mbar_wait(kv_full + 8 * st, (i >> 1) & 1)) { ok = false; break; }
-                if (first && !mbar_wait(q_ready, turn & 1)) { ok = false; break; }
+        for (; ts.valid; ts.next(p, it, lane), ++i) {
+            const int ks = i % KSTAGES, vs = i & 1;
+            const bool first = ts.first();
+            if (!mbar_wait(k_full + 8 * ks, (i / KSTAGES) & 1)) { ok = false; break; }
+            PF_TR(i, 1);
+            if (first && !mbar_wait(q_ready, turn & 1)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(0, ks);
+            if (i > 0) {
+                if (!mbar_wait(p_full + 8, (i - 1) & 1)) { ok = false; break; }
+                PF_TR(i - 1, 2);
                 tc_fence_after();
-                issue_s(0, st);
-                if (i > 0) {
-                    if (!mbar_wait(p_full + 8, (i - 1) & 1)) { ok = false; break; }
-                    tc_fence_after();
-                    issue_pv(1, prev_st, i - 1 > 0);
-                    if (lane == 0) umma_commit(kv_empty + 8 * prev_st);
-                    __syncwarp();
-                }
-                if (first && !mbar_wait(q_ready + 8, turn & 1)) { ok = false; break; }
-                tc_fence_after();
-                issue_s(1, st);
-                if (!mbar_wait(p_full, i & 1)) { ok = false; break; }
-                tc_fence_after();
-                issue_pv(0, st, i > 0);
-                prev_st = st;
+                issue_pv(1, vs ^ 1, i - 1 > 0);
+                commit(v_empty + 8 * (vs ^ 1));
             }
-            if (vmax > 0) ++turn;
-            off += __ldg(p.L + f);
+            if (first && !mbar_wait(q_ready + 8, turn & 1)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(1, ks);
+            commit(k_empty + 8 * ks);
+            if (!mbar_wait(v_full + 8 * vs, (i >> 1) & 1)) { ok = false; break; }
+            if (!mbar_wait(p_full, i & 1)) { ok = false; break; }
+            PF_TR(i, 3);
+            tc_fence_after();
+            issue_pv(0, vs, i > 0);
+            if (first) ++turn;
         }
         if (ok && i > 0) {
             if (mbar_wait(p_full + 8, (i - 1) & 1)) {
                 tc_fence_after();
-                issue_pv(1, prev_st, i - 1 > 0);
+                issue_pv(1, (i - 1) & 1, i - 1 > 0);
             } else {
                 ok = false;
             }
@@ -415,13 +501,15 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         const float sl2 = p.scale_log2;
         const uint32_t qtile = (uint32_t)(OFF_Q + grp * TILE);
         float m = neg_inf(), l = 0.f;  // running max (log2 units, stepped) and sum
-        int i = 0, off = 0;
+        int i = 0;
         bool ok = true;
         const int hp = p.R >> 1;
-        for (int f = 0; f < p.F && ok; ++f) {
-            const int L = __ldg(p.L + f);
-            const int vmax = item_span(p, it, f, off, lane);
-            if (vmax > 0) {
+        TileSeq ts;
+        ts.init(p, it, lane);
+        int lim = 0, vend = 0;
+        for (; ts.valid; ts.next(p, it, lane), ++i) {
+            const int f = ts.f, off = ts.off, win = ts.win, st = i & 1;
+            if (ts.first()) {
                 // ---- rotate this row's q for turn f into the A tile (in place) ----
                 const T* qrow = static_cast<const T*>(p.q) + ((size_t)t * p.Hq + hq) * E;
 #pragma unroll
@@ -457,17 +545,21 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                 fence_proxy_async_smem();
                 mbar_arrive(q_ready + 8 * grp);
                 // visible window of this row in turn f: logical positions [off, lim]
-                const int lim = row_ok ? off + turn_vis_pf(L, __ldg(p.loc + (size_t)f * p.T + t), off, p.cap) - 1 : off - 1;
-                const int vend = off + vmax;
-                for (int win = off & ~(KT - 1); win < off + vmax; win += KT, ++i) {
-                    const int st = i & 1;
+                lim = row_ok ? off + turn_vis_pf(__ldg(p.L + f), __ldg(p.loc + (size_t)f * p.T + t), off, p.cap) - 1
+                             : off - 1;
+                vend = off + ts.vmax;
+            }
+            {
+                {
                     if (!mbar_wait(s_full + 8 * grp, i & 1)) { ok = false; break; }
+                    if ((wid & 3) == 0) PF_TR(i, 4 + 2 * grp);
                     tc_fence_after();
                     float sv[KT];
 #pragma unroll
                     for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
                     tmem_wait_ld();
                     reg_fence<KT>(sv);
+                    if ((wid & 3) == 0) PF_TR(i, 8 + 4 * grp);
                     const int lo = off - win, hi = lim - win;  // visible columns [lo, hi]
                     if (!__all_sync(0xffffffffu, lo <= 0 && hi >= KT - 1)) {
 #pragma unroll
@@ -501,6 +593,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                     }
                     l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
                     m = mnew;
+                    if ((wid & 3) == 0) PF_TR(i, 9 + 4 * grp);
                     if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                         // O holds the PV of every earlier window (their MMAs completed
                         // before S of this window was signalled)
@@ -515,9 +608,11 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                             tmem_st32(tO + 32 * c, ov);
                         }
                     }
-                    if (grp == 0) {
+                    if ((wid & 3) == 0) PF_TR(i, 10 + 4 * grp);
+                    if (grp == 0 && (win < off || win + KT > vend)) {
                         // V rows of this window outside [off, vend) may hold another turn's
                         // or uninitialised pool data: zero them (P is 0 there, 0 * NaN is NaN)
+                        if (!mbar_wait(v_full + 8 * st, (i >> 1) & 1)) { ok = false; break; }
                         const int pos = win + r;
                         if (pos < off || pos >= vend) {
                             uint8_t* vrow = smem + OFF_V + st * TILE + r * 128;
@@ -531,10 +626,10 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                     }
                     tmem_wait_st();
                     tc_fence_before();
+                    if ((wid & 3) == 0) PF_TR(i, 5 + 2 * grp);
                     mbar_arrive(p_full + 8 * grp);
                 }
             }
-            off += L;
         }
         if (!ok && lane == 0) {
             *sAbort = 1;
@@ -629,7 +724,7 @@ size_t prefill_workspace_size(const dvattn_varlen_args* v) {
     return 256 + sizeof(pf::Item) * (size_t)prefill_max_items(v);
 }
 
-int prefill_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, cudaStream_t stream) {
+int prefill_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
     const size_t need = prefill_workspace_size(v);
     if (!workspace || wbytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) return DVATTN_ERR_WORKSPACE;
     pf::Params p{};
@@ -649,7 +744,8 @@ int prefill_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, 
 
     const size_t prep_smem = (sizeof(long long) + 4 * sizeof(int)) * ((size_t)p.W + 1);
     if (prep_smem > 48 * 1024) return DVATTN_ERR_UNSUPPORTED;
-    pf::prefill_prep_kernel<<<1, 1024, prep_smem, stream>>>(p);
+    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) pf::prefill_prep_kernel<<<1, 1024, prep_smem, stream>>>(p);
+    if (phase != DVATTN_PHASE_ALL && phase != DVATTN_PHASE_ATTEND) return cudaGetLastError() == cudaSuccess ? DVATTN_OK : DVATTN_ERR_CUDA;
 
     alignas(64) CUtensorMap mk, mv;
     const long long tokens = p.NB * p.BS;

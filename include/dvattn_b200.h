@@ -166,6 +166,14 @@ int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace,
                              size_t workspace_bytes, dvattn_stream_t stream);
 
 /*
+ * One phase of dvattn_varlen_paged_sdpa (see dvattn_paged_sdpa_phase).  On the tensor-core
+ * prefill path SCHEDULE builds the work list, ATTEND runs the attention kernel and MERGE
+ * has nothing to do.
+ */
+int dvattn_varlen_paged_sdpa_phase(const dvattn_varlen_args* args, void* workspace,
+                                   size_t workspace_bytes, int phase, dvattn_stream_t stream);
+
+/*
  * Standalone query rotation, schema `dvattn_rope` (src/binding.cu:41-77, src/rope.cuh:2-65):
  * out [F,W,Hq,S,E] T = rotate(queries [W,Hq,S,E] T, cos/sin [F,W,S,R] f32).
  */

@@ -135,3 +135,18 @@ def test_prefill_repeatable(prefill_mode):
     b = run(c)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("mode", ["1", "0"])
+def test_varlen_phases_equal_whole_call(prefill_mode, mode):
+    prefill_mode(mode)
+    c = wl.make_varlen([[400], [150]], [96, 150], Hq=32, Hkv=2, E=128, R=32, BS=16, dtype=torch.bfloat16, seed=14)
+    g = c.to(DEV)
+    a = g.new_out()
+    b = g.new_out()
+    capi.VarlenCall(*g.capi_args(a))()
+    call = capi.VarlenCall(*g.capi_args(b))
+    for ph in (capi.DVATTN_PHASE_SCHEDULE, capi.DVATTN_PHASE_ATTEND, capi.DVATTN_PHASE_MERGE):
+        call.phase(ph)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
