@@ -27,6 +27,7 @@
 #include "decode.cuh"
 #include "tma_host.cuh"
 
+#include <cstdio>
 #include <cstdlib>
 
 namespace dvb {
@@ -149,6 +150,29 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b), "r"(id), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
         : "memory");
+}
+// Packed f32x2 arithmetic (one instruction for two lanes of a 64-bit register pair) and a
+// three-input max, both native on sm_100.
+__device__ __forceinline__ uint64_t f2u(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void u2f(uint64_t r, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r)); }
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -570,28 +594,40 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
 #pragma unroll
                     for (int u = 0; u < 8; ++u) mx[u] = sv[u];
 #pragma unroll
-                    for (int c = 8; c < KT; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
-                    const float mxs = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                            fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+                    for (int c = 8; c < KT; c += 16)
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) mx[u] = fmax3(mx[u], sv[c + u], sv[c + 8 + u < KT ? c + 8 + u : c + u]);
+                    const float mxs = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * sl2;
                     // the reference point moves only when the max grows by more than 8
                     // (a factor 256 in the exponentials); the result is exact either way
                     const float mnew = mxs > m + 8.f ? mxs : m;
                     const float alpha = mnew == m ? 1.f : ex2(m - mnew);
                     const float mu = mnew == neg_inf() ? 0.f : mnew;
-                    float ps[4] = {0.f, 0.f, 0.f, 0.f};
+                    const uint64_t sc2 = f2u(sl2, sl2), nmu2 = f2u(-mu, -mu);
+                    uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
                     for (int c = 0; c < KT / 32; ++c) {
                         uint32_t pk[16];
 #pragma unroll
                         for (int u = 0; u < 16; ++u) {
-                            const float e0 = ex2(fmaf(sv[32 * c + 2 * u], sl2, -mu));
-                            const float e1 = ex2(fmaf(sv[32 * c + 2 * u + 1], sl2, -mu));
-                            ps[u & 3] += e0 + e1;
+                            float x0, x1;
+                            u2f(ffma2(f2u(sv[32 * c + 2 * u], sv[32 * c + 2 * u + 1]), sc2, nmu2), x0, x1);
+                            const float e0 = ex2(x0), e1 = ex2(x1);
+                            const uint64_t e2 = f2u(e0, e1);
+                            ps2[u & 3] = fadd2(ps2[u & 3], e2);
                             pk[u] = Elem<T>::pack2(e0, e1);
                         }
                         tmem_st16(tS + 16 * c, pk);
                     }
-                    l = l * alpha + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+                    float psum;
+                    {
+                        float a0, a1, b0, b1;
+                        u2f(fadd2(fadd2(ps2[0], ps2[1]), fadd2(ps2[2], ps2[3])), a0, a1);
+                        (void)b0;
+                        (void)b1;
+                        psum = a0 + a1;
+                    }
+                    l = l * alpha + psum;
                     m = mnew;
                     if ((wid & 3) == 0) PF_TR(i, 9 + 4 * grp);
                     if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -757,8 +793,11 @@ int prefill_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, 
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::SMEM) != cudaSuccess)
         return DVATTN_ERR_CUDA;
     void* args[] = {&p, &mk, &mv};
-    if (cudaLaunchKernel(fn, dim3(p.max_items), dim3(pf::NT), args, pf::SMEM, stream) != cudaSuccess)
+    const cudaError_t e = cudaLaunchKernel(fn, dim3(p.max_items), dim3(pf::NT), args, pf::SMEM, stream);
+    if (e != cudaSuccess) {
+        if (getenv("DVATTN_DEBUG")) fprintf(stderr, "dvattn prefill launch: %s\n", cudaGetErrorString(e));
         return DVATTN_ERR_CUDA;
+    }
     return cudaGetLastError() == cudaSuccess ? DVATTN_OK : DVATTN_ERR_CUDA;
 }
 
