@@ -1569,6 +1569,8 @@ template <class T, int E>
 __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p) {
     constexpr int C4 = E / 4, NTH = 16 * C4, B = 8;
     // launched as a programmatic dependent of the attention kernel: wait for its results
+    // let the next call's schedule kernel start its (read-only) work now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int g_seg = blockIdx.x;
     const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
@@ -1870,7 +1872,21 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.n_launch = n_launch;
     p.min_units = kc.min_units;
 
-    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) decode_prep_kernel<<<1, 1024, 0, stream>>>(p);
+    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) {
+        // programmatic dependent of whatever precedes it (the previous call's merge): it
+        // computes the schedule before waiting, and writes it after
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1);
+        cfg.blockDim = dim3(1024);
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        void* pargs[] = {&p};
+        if (cudaLaunchKernelExC(&cfg, (const void*)&decode_prep_kernel, pargs) != cudaSuccess) return DVATTN_ERR_CUDA;
+    }
     if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_ATTEND) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(n_launch);

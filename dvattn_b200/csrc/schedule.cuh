@@ -108,8 +108,15 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
     __shared__ long long carry_s;
     constexpr int kSharedRows = 2048;  // rows whose prefix sums are also kept in shared memory
     __shared__ long long sP[kSharedRows + 1];
+    constexpr int kSharedCtas = 2048;  // CTA boundaries computed before the wait below
+    __shared__ long long sC[kSharedCtas + 1];
     // let the attention kernel launch now; it waits (griddepcontrol.wait) for our results
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // This kernel is itself a programmatic dependent of the previous call's merge, which
+    // still reads the workspace: everything up to the writes is computed before waiting
+    // for it (when the rows fit in shared memory), so that work overlaps the merge.
+    const bool early = p.WS <= kSharedRows;
+    if (!early) asm volatile("griddepcontrol.wait;" ::: "memory");
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     if (tid == 0) carry_s = 0;
     __syncthreads();
@@ -138,38 +145,23 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
         const long long carry = carry_s;
         const long long excl = carry + (wid ? warp_tot[wid - 1] : 0) + x - v;
         if (ws < p.WS) {
-            p.P[ws] = excl;
+            if (!early) p.P[ws] = excl;
             if (ws <= kSharedRows) sP[ws] = excl;
         }
         __syncthreads();
         if (tid == 1023) carry_s = excl + v;
         __syncthreads();
     }
-    if (p.cu_q) {
-        // sequence of each packed token: the first w with t < cu[w+1]
-        // (src/kernels/varlen_paged_kernel_v21.cuh:40-47), 0 if there is none.
-        for (int t = tid; t < p.WS; t += 1024) {
-            int lo = 0, hi = p.nseq;  // search in [lo, hi)
-            while (lo < hi) {
-                const int mid = (lo + hi) >> 1;
-                if (t < __ldg(p.cu_q + mid + 1)) hi = mid; else lo = mid + 1;
-            }
-            p.row_seq[t] = lo < p.nseq ? lo : 0;
-        }
-    }
     __shared__ int n_s;
     __shared__ long long U_s;
     if (tid == 0) {
         const long long tot = carry_s;
-        p.P[p.WS] = tot;
+        if (!early) p.P[p.WS] = tot;
         if (p.WS <= kSharedRows) sP[p.WS] = tot;
         const long long U = tot * p.hsplit;
         long long want = (U + p.min_units - 1) / p.min_units;
         int n = (int)(want < p.n_launch ? want : p.n_launch);
         n = U > 0 ? (n > 0 ? n : 1) : 0;
-        p.sched->U = U;
-        p.sched->error = 0;
-        p.sched->n_eff = n;
         n_s = n;
         U_s = U;
     }
@@ -180,6 +172,7 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
     const int n = n_s;
     const long long U = U_s;
     const long long* Pq = p.WS <= kSharedRows ? sP : p.P;
+    if (early && n > kSharedCtas) asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int c = tid; c <= n; c += 1024) {
         long long u = (n > 0) ? (long long)c * U / n : 0;
         if (c > 0 && c < n) {
@@ -210,7 +203,37 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
                 }
             }
         }
-        p.cstart[c] = (c == n) ? U : u;
+        const long long cs = (c == n) ? U : u;
+        if (early && n <= kSharedCtas) sC[c] = cs; else p.cstart[c] = cs;
+        if (c == 0 && !early) {
+            p.sched->U = U;
+            p.sched->error = 0;
+            p.sched->n_eff = n;
+        }
+    }
+    if (early) {
+        __syncthreads();
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        for (int ws = tid; ws <= p.WS; ws += 1024) p.P[ws] = sP[ws];
+        if (n <= kSharedCtas)
+            for (int c = tid; c <= n; c += 1024) p.cstart[c] = sC[c];
+        if (tid == 0) {
+            p.sched->U = U;
+            p.sched->error = 0;
+            p.sched->n_eff = n;
+        }
+    }
+    if (p.cu_q) {  // after the wait in both modes
+        // sequence of each packed token: the first w with t < cu[w+1]
+        // (src/kernels/varlen_paged_kernel_v21.cuh:40-47), 0 if there is none.
+        for (int t = tid; t < p.WS; t += 1024) {
+            int lo = 0, hi = p.nseq;  // search in [lo, hi)
+            while (lo < hi) {
+                const int mid = (lo + hi) >> 1;
+                if (t < __ldg(p.cu_q + mid + 1)) hi = mid; else lo = mid + 1;
+            }
+            p.row_seq[t] = lo < p.nseq ? lo : 0;
+        }
     }
 }
 
