@@ -254,6 +254,8 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
     float* sLse = sML + WARPS * 16 * 2; // [16]
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    // the merge kernel may launch now: its CTAs wait (griddepcontrol.wait) for this grid
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // programmatic dependent of the schedule kernel: wait for its header and prefix sums
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
@@ -570,6 +572,8 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    // the merge kernel may launch now: its CTAs wait (griddepcontrol.wait) for this grid
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // programmatic dependent of the schedule kernel: wait for its header and prefix sums
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
@@ -943,6 +947,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     // smem [page chunk][head][panel][boxr rows][128 B].
     const int boxr_shift = __ffs(boxr) - 1;
     const uint32_t box_bytes = (uint32_t)Hkv * NPANEL * boxr * 128u;
+    // the merge kernel may launch now: its CTAs wait (griddepcontrol.wait) for this grid
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // programmatic dependent of the schedule kernel: wait for its header and prefix sums
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
@@ -1375,6 +1381,8 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
     float* sP = sQ + 16 * LD;
 
     const int tid = threadIdx.x;
+    // the merge kernel may launch now: its CTAs wait (griddepcontrol.wait) for this grid
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // programmatic dependent of the schedule kernel: wait for its header and prefix sums
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const DecodeSched sch = *p.sched;
@@ -1575,8 +1583,17 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     const int g_seg = blockIdx.x;
     const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
     const int tid = threadIdx.x, r = tid / C4, c4 = tid - r * C4;
+    // The CTA boundaries are searched twice below: stage them in shared memory with one
+    // round of parallel loads instead of a chain of dependent global loads.
+    constexpr int kMaxC = 1024;
+    __shared__ long long s_cs[kMaxC + 1];
+    const bool cs_shared = p.n_launch <= kMaxC;
+    if (cs_shared)
+        for (int i = tid; i <= p.n_launch; i += NTH) s_cs[i] = p.cstart[i];
     const DecodeSched sch = *p.sched;
     const long long P0 = p.P[ws], V = p.P[ws + 1] - P0;
+    __syncthreads();
+    const long long* cst = cs_shared ? s_cs : p.cstart;
     const int w = ws / p.S, s = ws - w * p.S;
     const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
     if (V == 0) {
@@ -1589,12 +1606,12 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     }
     const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
     const int n = sch.n_eff;
-    const int ca = cta_of(p.cstart, b, n), cb = cta_of(p.cstart, b + V - 1, n);
+    const int ca = cta_of(cst, b, n), cb = cta_of(cst, b + V - 1, n);
     if (ca == cb) return;
     __shared__ int s_part[NTH];
     const int npc = cb - ca + 1;
     const int hh = p.slot_heads > 1 ? hkv : 0;
-    const bool ca_not_first = p.cstart[ca] < b;
+    const bool ca_not_first = cst[ca] < b;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float M = neg_inf(), den = 0.f;
     for (int base = 0; base < npc; base += NTH) {
@@ -1604,7 +1621,7 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
             const int cc = ca + base + tid;
             const int slot = (cc == ca && ca_not_first) ? 2 * ca + 1 : 2 * cc;
             // a CTA whose range is empty (boundaries snapped together) wrote no piece
-            s_part[tid] = p.cstart[cc] == p.cstart[cc + 1] ? -1 : (slot * p.slot_heads + hh) * 16;
+            s_part[tid] = cst[cc] == cst[cc + 1] ? -1 : (slot * p.slot_heads + hh) * 16;
         }
         __syncthreads();
         if (r >= p.gqa) continue;
