@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
     for (int i = tid; i < 16 * E; i += NT) sO[i] = 0.f;
 
     TileIter<TILE> prod, cons;
-    prod.init(p, ws0, u0, u1);
+    prod.init(p, ws0, p.P[ws0], u0, u1);
     cons = prod;
 #pragma unroll
     for (int st = 0; st < STAGES - 1; ++st) {
@@ -601,7 +601,7 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
             prefetch_tmap(&tmv);
         }
         TileIter<TILE> it;
-        it.init(p, ws0, u0, u1);
+        it.init(p, ws0, p.P[ws0], u0, u1);
         it.align = TILE;
         const uint32_t box_bytes = (uint32_t)boxr * 128u;
         int i = 0;
@@ -885,6 +885,19 @@ __global__ void __launch_bounds__(160, (E <= 128) ? 2 : 1) decode_tma_kernel(Pag
     }
 }
 
+// four consecutive output elements (8-byte store for 16-bit types, 16-byte for f32)
+template <class T> __device__ __forceinline__ void store_quad(T* dst, float a, float b, float c, float d) {
+    uint2 pk;
+    pk.x = Elem<T>::pack2(a, b);
+    pk.y = Elem<T>::pack2(c, d);
+    *reinterpret_cast<uint2*>(dst) = pk;
+}
+template <> __device__ __forceinline__ void store_quad<float>(float* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+}
+
+
+
 // ==================================================================================
 // Row kernel (f16 / bf16, Hkv | CW): like the TMA kernel, but a CTA streams ALL KV heads
 // of its keys.  A stage holds TOKB = 16*CW/Hkv keys x Hkv heads; consumer warp w serves
@@ -926,6 +939,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     extern __shared__ __align__(1024) uint8_t smem[];
     const uint32_t s0 = smem_u32(smem);
     if (s0 & 1023) {  // the 128-byte TMA swizzle pattern needs 1024-byte aligned stages
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         if (threadIdx.x == 0) atomicOr(&p.sched->error, 4);
         return;
     }
@@ -949,14 +963,52 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     const uint32_t box_bytes = (uint32_t)Hkv * NPANEL * boxr * 128u;
     // the merge kernel may launch now: its CTAs wait (griddepcontrol.wait) for this grid
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    // programmatic dependent of the schedule kernel: wait for its header and prefix sums
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const DecodeSched sch = *p.sched;
     const int c = blockIdx.x;
-    if (c >= sch.n_eff) return;
-    const long long u0 = p.cstart[c], u1 = p.cstart[c + 1];
-    if (u0 >= u1) return;
-    const int ws0 = find_row<C::NT>(p, u0);
+    long long u0, u1, P0, U = 0, pubP = 0;
+    int ws0, n = 0;
+    // fused schedule, producer warp: after the previous grid completed, publish P, cstart
+    // and the header for the merge kernel
+    auto publish = [&]() {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (32 * c + lane <= p.WS) p.P[32 * c + lane] = pubP;
+        if (lane == 0 && c < n) {
+            p.cstart[c] = u0;
+            if (c == n - 1) p.cstart[n] = U;
+        }
+        if (lane == 0 && c == 0) {
+            p.sched->U = U;
+            p.sched->n_eff = n;
+        }
+    };
+    if (p.fused) {
+        // In-kernel schedule (no prep kernel): every CTA scans the row unit counts into the
+        // K/V stages (unused until the first TMA) and finds its own range.  Only inputs
+        // are read here, so this and the streaming below overlap the previous grid; the
+        // first global write of every warp comes after griddepcontrol.wait.
+        long long* sP = reinterpret_cast<long long*>(smem);
+        cta_prefix<C::NT>(p, sP, sP + p.WS + 1, U, n);
+        u0 = cta_boundary(p, sP, U, n, c);
+        u1 = cta_boundary(p, sP, U, n, c + 1);
+        ws0 = u0 < u1 ? find_row_in(sP, p.WS, p.hsplit, u0) : 0;
+        P0 = sP[ws0];
+        // this CTA publishes P[32c .. 32c+31] (producer warp lanes)
+        if (wid == CW && 32 * c + lane <= p.WS) pubP = sP[32 * c + lane];
+        __syncthreads();
+        if (u0 >= u1) {
+            if (wid == CW) publish();
+            return;
+        }
+    } else {
+        // programmatic dependent of the schedule kernel: wait for its header and prefix sums
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        const DecodeSched sch = *p.sched;
+        if (c >= sch.n_eff) return;
+        u0 = p.cstart[c];
+        u1 = p.cstart[c + 1];
+        if (u0 >= u1) return;
+        ws0 = find_row<C::NT>(p, u0);
+        P0 = p.P[ws0];
+    }
 
     if (tid == 0) {
         for (int st = 0; st < STAGES; ++st) {
@@ -975,7 +1027,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             prefetch_tmap(&tmv);
         }
         TileIter<64> it;
-        it.init(p, ws0, u0, u1);
+        it.init(p, ws0, P0, u0, u1);
         it.align = TOKB;
         struct Pend {
             TileDesc d;
@@ -1053,6 +1105,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                 tma_load_4d(sV0 + off, &tmv, 0, z, 0, 0, bar_full + st * 8);
             }
         }
+        if (p.fused) publish();
         if (!ok) {
             if (lane == 0) {
                 *sAbort = 1;
@@ -1082,7 +1135,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     // loads are in flight, instead of after they land.
     {
         TileIter<64> it0;
-        it0.init(p, ws0, u0, u1);
+        it0.init(p, ws0, P0, u0, u1);
         it0.align = TOKB;
         TileDesc d0;
         if (it0.next(p, d0)) {
@@ -1104,6 +1157,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         const int st = i % STAGES;
         if (!mbar_wait(bar_full + st * 8, (i / STAGES) & 1)) {
             if (lane == 0) {
+                asm volatile("griddepcontrol.wait;" ::: "memory");
                 *sAbort = 1;
                 atomicOr(&p.sched->error, 2);
             }
@@ -1121,7 +1175,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
 #pragma unroll
             for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
         }
+#ifdef DVB_EXP_NOROT
+        if (false) {
+#else
         if ((d.flags & 2) && i > 0) {
+#endif
 #ifdef DVB_TRACE
             const unsigned long long tr0 = global_ns();
             if (tid == 0) DVB_TADD(6, tr0);
@@ -1143,7 +1201,11 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
 #endif
         }
 
+#ifdef DVB_EXP_NOMATH
+        const int lo = 0, hi = 0;
+#else
         const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
+#endif
         const uint32_t kb = sK0 + st * C::STAGE_BYTES;
         const uint32_t vb = sV0 + st * C::STAGE_BYTES;
         if (hi > lo) {
@@ -1231,6 +1293,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         if (lane == 0) mbar_arrive(bar_empty + st * 8);
 
         if (d.flags & 4) {
+            // first global writes of this warp: after the previous grid has completed
+            if (p.fused) asm volatile("griddepcontrol.wait;" ::: "memory");
             // ---- finish this row piece: per head, combine its wph warps ----
             float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
             lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
@@ -1421,7 +1485,7 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
     };
 
     TileIter<TILE> prod, cons;
-    prod.init(p, ws0, u0, u1);
+    prod.init(p, ws0, p.P[ws0], u0, u1);
     cons = prod;
 #pragma unroll
     for (int st = 0; st < STAGES - 1; ++st) {
@@ -1559,16 +1623,6 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
 // merge of split segments (and zeros for rows that see no key)
 // one CTA per segment, 128 threads: thread t -> row t/8, columns 4*((t%8) + 8k)
 // ==================================================================================
-// four consecutive output elements (8-byte store for 16-bit types, 16-byte for f32)
-template <class T> __device__ __forceinline__ void store_quad(T* dst, float a, float b, float c, float d) {
-    uint2 pk;
-    pk.x = Elem<T>::pack2(a, b);
-    pk.y = Elem<T>::pack2(c, d);
-    *reinterpret_cast<uint2*>(dst) = pk;
-}
-template <> __device__ __forceinline__ void store_quad<float>(float* dst, float a, float b, float c, float d) {
-    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
-}
 
 // One block per segment (ws, hkv), one thread per (query row r, 4-column group c4):
 // blockDim = 16 * E / 4.  Pieces are consumed in batches of 8 whose loads are all in
@@ -1675,6 +1729,7 @@ struct KernelChoice {
     bool tma = false;
     bool row = false;  // all KV heads per CTA (hsplit = 1)
     int cw = 4;
+    size_t sched_smem = 0;  // shared bytes the row kernel lends to its in-kernel schedule
 };
 
 template <class T, int E, int CW, int STAGES>
@@ -1683,6 +1738,7 @@ KernelChoice row_choice() {
     KernelChoice k{reinterpret_cast<const void*>(&decode_row_kernel<T, E, CW, STAGES>), C::SMEM, C::NT, 64, true};
     k.row = true;
     k.cw = CW;
+    k.sched_smem = 2 * C::OFF_V;
     return k;
 }
 
@@ -1888,8 +1944,13 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     }
     p.n_launch = n_launch;
     p.min_units = kc.min_units;
+    // Row kernel on paged decode: the split is computed inside the attention kernel (its
+    // stages hold the prefix sums; CTA c publishes P[32c..32c+31] for the merge), so no
+    // prep kernel runs and a call's streaming starts while the previous call's merge runs.
+    p.fused = (kc.row && !p.cu_q && (size_t)(p.WS + 1 + 32) * 8 <= kc.sched_smem &&
+               (long long)p.WS + 1 <= 32LL * n_launch) ? 1 : 0;
 
-    if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) {
+    if ((phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) && !p.fused) {
         // programmatic dependent of whatever precedes it (the previous call's merge): it
         // computes the schedule before waiting, and writes it after
         cudaLaunchConfig_t cfg = {};

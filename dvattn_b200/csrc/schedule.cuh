@@ -64,7 +64,12 @@ struct PagedParams {
     int bs_shift;      // log2(block_size) when it is a power of two, else -1
     long long* cstart; // [n_launch + 1] first unit of each CTA's range (written by the prep kernel)
     int rot_units;     // units charged for a turn start (its query rotation) in the balanced split
+    // 1: no prep kernel; every attention CTA computes the split itself (cta_prefix /
+    // cta_boundary) and publishes its share of P / cstart / the header for the merge
+    int fused;
 };
+
+
 
 __device__ __forceinline__ int row_block_table(const PagedParams& p, int ws) {
     return p.cu_q ? p.row_seq[ws] : ws / p.S;
@@ -103,6 +108,83 @@ __device__ __forceinline__ int cta_of(const long long* cstart, long long u, int 
 }
 
 // One pass over the schedule: fills P and the header.  Single CTA of 1024 threads.
+// First unit of CTA c of n: c * U / n, moved back to the start of a turn when it falls
+// inside the rotation units of that turn, so every turn's rotation is done by the CTA that
+// streams the turn's first keys.  Pq: the prefix sums P (shared or global memory).
+__device__ __forceinline__ long long cta_boundary(const PagedParams& p, const long long* Pq, long long U, int n, int c) {
+    if (c >= n) return U;
+    long long u = (n > 0) ? (long long)c * U / n : 0;
+    if (c > 0) {
+        int lo = 0, hi = p.WS - 1;  // row: largest ws with P[ws] * hsplit <= u
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (Pq[mid] * p.hsplit <= u) lo = mid; else hi = mid - 1;
+        }
+        const int ws = lo;
+        const long long V = Pq[ws + 1] - Pq[ws];
+        if (V > 0) {
+            const long long r = u - Pq[ws] * p.hsplit;
+            long long acc = (r / V) * V;  // start of the segment (KV head) within the row
+            int off = 0;
+            for (int f = 0; f < p.F; ++f) {
+                const int L = __ldg(p.L + f);
+                const int tu = turn_units(turn_vis(L, __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap), p.rot_units);
+                // (turn start, end of its rotation units]: snap to the turn start, so a
+                // non-empty range holding a turn's rotation units also holds its first key
+                if (tu > 0 && r <= acc + p.rot_units) {
+                    u -= r - acc;
+                    break;
+                }
+                if (r < acc + tu) break;
+                acc += tu;
+                off += L;
+            }
+        }
+    }
+    return u;
+}
+
+// Number of CTAs that own units: ceil(U / min_units) capped at n_launch (>= 1 if U > 0).
+__device__ __forceinline__ int sched_ctas(const PagedParams& p, long long U) {
+    const long long want = (U + p.min_units - 1) / p.min_units;
+    int n = (int)(want < p.n_launch ? want : p.n_launch);
+    return U > 0 ? (n > 0 ? n : 1) : 0;
+}
+
+// In-kernel schedule (PagedParams::fused): block-wide exclusive scan of the row unit
+// counts into sP[0..WS] (shared memory), then U and the CTA count.  All threads of the
+// block call it; sP must hold WS + 1 entries.
+template <int NT>
+__device__ __forceinline__ void cta_prefix(const PagedParams& p, long long* sP, long long* sScratch, long long& U,
+                                           int& n) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    constexpr int NW = NT / 32;
+    long long carry = 0;
+    for (int base = 0; base < p.WS; base += NT) {
+        const int ws = base + tid;
+        const long long v = ws < p.WS ? (long long)seg_visible(p, ws) : 0;
+        long long x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) sScratch[wid] = x;
+        __syncthreads();
+        long long before = carry;
+        for (int w2 = 0; w2 < wid; ++w2) before += sScratch[w2];
+        if (ws < p.WS) sP[ws] = before + x - v;
+        long long tot = carry;
+        for (int w2 = 0; w2 < NW; ++w2) tot += sScratch[w2];
+        carry = tot;
+        __syncthreads();
+    }
+    if (tid == 0) sP[p.WS] = carry;
+    U = carry * p.hsplit;
+    n = sched_ctas(p, U);
+    __syncthreads();
+}
+
 __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
     __shared__ long long warp_tot[32];
     __shared__ long long carry_s;
@@ -159,51 +241,19 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
         if (!early) p.P[p.WS] = tot;
         if (p.WS <= kSharedRows) sP[p.WS] = tot;
         const long long U = tot * p.hsplit;
-        long long want = (U + p.min_units - 1) / p.min_units;
-        int n = (int)(want < p.n_launch ? want : p.n_launch);
-        n = U > 0 ? (n > 0 ? n : 1) : 0;
+        const int n = sched_ctas(p, U);
         n_s = n;
         U_s = U;
     }
     __syncthreads();
     // CTA boundaries: c * U / n, moved back to the start of a turn when they fall inside
-    // the rotation units of that turn, so every turn's rotation is done by the CTA that
-    // streams the turn's first keys.
+    // the rotation units of that turn (cta_boundary).
     const int n = n_s;
     const long long U = U_s;
     const long long* Pq = p.WS <= kSharedRows ? sP : p.P;
     if (early && n > kSharedCtas) asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int c = tid; c <= n; c += 1024) {
-        long long u = (n > 0) ? (long long)c * U / n : 0;
-        if (c > 0 && c < n) {
-            int lo = 0, hi = p.WS - 1;  // row: largest ws with P[ws] * hsplit <= u
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (Pq[mid] * p.hsplit <= u) lo = mid; else hi = mid - 1;
-            }
-            const int ws = lo;
-            const long long V = Pq[ws + 1] - Pq[ws];
-            if (V > 0) {
-                const long long r = u - Pq[ws] * p.hsplit;
-                long long acc = (r / V) * V;  // start of the segment (KV head) within the row
-                int off = 0;
-                for (int f = 0; f < p.F; ++f) {
-                    const int L = __ldg(p.L + f);
-                    const int tu = turn_units(turn_vis(L, __ldg(p.loc + (size_t)f * p.WS + ws), off, p.cap), p.rot_units);
-                    // (turn start, end of its rotation units]: snap to the turn start, so
-                    // a non-empty range holding a turn's rotation units also holds its
-                    // first key
-                    if (tu > 0 && r <= acc + p.rot_units) {
-                        u -= r - acc;
-                        break;
-                    }
-                    if (r < acc + tu) break;
-                    acc += tu;
-                    off += L;
-                }
-            }
-        }
-        const long long cs = (c == n) ? U : u;
+        const long long cs = cta_boundary(p, Pq, U, n, c);
         if (early && n <= kSharedCtas) sC[c] = cs; else p.cstart[c] = cs;
         if (c == 0 && !early) {
             p.sched->U = U;
@@ -255,15 +305,15 @@ template <int TILE> struct TileIter {
     bool from_start, pend_seg, pend_turn, first_seg;
     int align;
 
-    __device__ __forceinline__ int seg_len(const PagedParams& p, int w) const {
-        return (int)(p.P[w + 1] - p.P[w]);
-    }
+    // units of row w (= P[w + 1] - P[w]), from the inputs: the iterator never reads P, so
+    // it also runs under the in-kernel schedule, where P is published only at the end
+    __device__ __forceinline__ int seg_len(const PagedParams& p, int w) const { return seg_visible(p, w); }
 
-    // ws0: segment row containing u0 (found by the caller); u0/u1: unit range.
-    __device__ __forceinline__ void init(const PagedParams& p, int ws0, long long u0, long long u1) {
+    // ws0: segment row containing u0 and P0 = P[ws0] (found by the caller); u0/u1: unit range.
+    __device__ __forceinline__ void init(const PagedParams& p, int ws0, long long P0, long long u0, long long u1) {
         ws = ws0;
         const int V = seg_len(p, ws);
-        long long r = u0 - p.P[ws] * p.hsplit;
+        long long r = u0 - P0 * p.hsplit;
         hkv = (int)(r / V);
         int ts = (int)(r - (long long)hkv * V);
         seg_left = V - ts;
@@ -304,7 +354,7 @@ template <int TILE> struct TileIter {
                 off = 0;
                 if (++hkv == p.hsplit) {
                     hkv = 0;
-                    do { ++ws; } while (p.P[ws + 1] == p.P[ws]);
+                    do { ++ws; } while (seg_visible(p, ws) == 0);
                 }
                 seg_left = seg_len(p, ws);
                 from_start = true;
@@ -341,6 +391,14 @@ template <int TILE> struct TileIter {
 
 // Segment row containing unit u0: the largest ws with P[ws] * Hkv <= u0 (so empty rows
 // before a non-empty one are skipped).  Block-wide; all threads get the result.
+__device__ __forceinline__ int find_row_in(const long long* Pq, int WS, int hsplit, long long u0) {
+    int lo = 0, hi = WS - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (Pq[mid] * hsplit <= u0) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
 template <int NT>
 __device__ __forceinline__ int find_row(const PagedParams& p, long long u0) {
     int cnt = 0;
