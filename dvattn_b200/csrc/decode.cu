@@ -1624,30 +1624,16 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
 // one CTA per segment, 128 threads: thread t -> row t/8, columns 4*((t%8) + 8k)
 // ==================================================================================
 
-// One block per segment (ws, hkv), one thread per (query row r, 4-column group c4):
-// blockDim = 16 * E / 4.  Pieces are consumed in batches of 8 whose loads are all in
-// flight before any is used (the merge is latency-bound, not bandwidth-bound).
+// Merge of one (row, KV head) segment, one thread per (query row r, 4-column group c4):
+// blockDim = 16 * E / 4; all threads of the block call it with the same segment.  Pieces
+// are consumed in batches of 16 whose loads are all in flight before any is used (the
+// merge is latency-bound, not bandwidth-bound).
 template <class T, int E>
-__global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p) {
-    constexpr int C4 = E / 4, NTH = 16 * C4, B = 8;
-    // launched as a programmatic dependent of the attention kernel: wait for its results
-    // let the next call's schedule kernel start its (read-only) work now
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int g_seg = blockIdx.x;
+__device__ __forceinline__ void merge_segment(const PagedParams& p, int g_seg, const long long* cst, int n, int* s_part) {
+    constexpr int C4 = E / 4, NTH = 16 * C4, B = 16;
     const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
     const int tid = threadIdx.x, r = tid / C4, c4 = tid - r * C4;
-    // The CTA boundaries are searched twice below: stage them in shared memory with one
-    // round of parallel loads instead of a chain of dependent global loads.
-    constexpr int kMaxC = 1024;
-    __shared__ long long s_cs[kMaxC + 1];
-    const bool cs_shared = p.n_launch <= kMaxC;
-    if (cs_shared)
-        for (int i = tid; i <= p.n_launch; i += NTH) s_cs[i] = p.cstart[i];
-    const DecodeSched sch = *p.sched;
     const long long P0 = p.P[ws], V = p.P[ws + 1] - P0;
-    __syncthreads();
-    const long long* cst = cs_shared ? s_cs : p.cstart;
     const int w = ws / p.S, s = ws - w * p.S;
     const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
     if (V == 0) {
@@ -1659,10 +1645,8 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
         return;
     }
     const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
-    const int n = sch.n_eff;
     const int ca = cta_of(cst, b, n), cb = cta_of(cst, b + V - 1, n);
     if (ca == cb) return;
-    __shared__ int s_part[NTH];
     const int npc = cb - ca + 1;
     const int hh = p.slot_heads > 1 ? hkv : 0;
     const bool ca_not_first = cst[ca] < b;
@@ -1714,6 +1698,31 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, acc.x, acc.y, acc.z, acc.w);
     if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = acc;
     if (p.lse_out && c4 == 0) p.lse_out[orow] = den > 0.f ? (M + __log2f(den)) * kLn2 : neg_inf();
+}
+
+// Grid-stride over the (row, KV head) segments: few blocks, so that while they wait for
+// the attention grid they hold few of the slots the next call's attention CTAs need.
+template <class T, int E>
+__global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p) {
+    constexpr int NTH = 16 * (E / 4);
+    // launched as a programmatic dependent of the attention kernel: wait for its results
+    // let the next call's schedule kernel start its (read-only) work now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int tid = threadIdx.x;
+    // The CTA boundaries are searched twice below: stage them in shared memory with one
+    // round of parallel loads instead of a chain of dependent global loads.
+    constexpr int kMaxC = 1024;
+    __shared__ long long s_cs[kMaxC + 1];
+    const bool cs_shared = p.n_launch <= kMaxC;
+    if (cs_shared)
+        for (int i = tid; i <= p.n_launch; i += NTH) s_cs[i] = p.cstart[i];
+    const DecodeSched sch = *p.sched;
+    __syncthreads();
+    const long long* cst = cs_shared ? s_cs : p.cstart;
+    __shared__ int s_part[NTH];
+    for (int g_seg = blockIdx.x; g_seg < p.WS * p.Hkv; g_seg += gridDim.x)
+        merge_segment<T, E>(p, g_seg, cst, sch.n_eff, s_part);
 }
 
 // ==================================================================================
@@ -2009,7 +2018,13 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
                 break;
         }
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)p.WS * (unsigned)p.Hkv);
+#ifndef DVB_MERGE_CTAS
+#define DVB_MERGE_CTAS 64
+#endif
+        // few blocks (grid-stride over the segments): they hold few of the slots the next
+        // call's attention CTAs need while they wait for this call's attention grid
+        const long long nseg = (long long)p.WS * p.Hkv;
+        cfg.gridDim = dim3((unsigned)(nseg < DVB_MERGE_CTAS ? nseg : DVB_MERGE_CTAS));
         cfg.blockDim = dim3(16 * p.E / 4);
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
