@@ -30,9 +30,11 @@ _load()
 
 from .api import (  # noqa: E402
     apply_rotary_pos_emb,
+    dvattn_fused,
     dvattn_lse_merge,
     dvattn_paged_sdpa,
     dvattn_rope,
+    dvattn_sdpa,
     dvattn_varlen_paged_sdpa,
     dvattn_varlen_rope,
     rotate_half,
@@ -40,9 +42,11 @@ from .api import (  # noqa: E402
 
 __all__ = [
     "apply_rotary_pos_emb",
+    "dvattn_fused",
     "dvattn_lse_merge",
     "dvattn_paged_sdpa",
     "dvattn_rope",
+    "dvattn_sdpa",
     "dvattn_varlen_paged_sdpa",
     "dvattn_varlen_rope",
     "rotate_half",

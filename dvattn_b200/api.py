@@ -1,7 +1,8 @@
-"""Python wrappers in the style of python/dvattn/attention.py (``dvattn_rope``,
-``rotate_half``, ``apply_rotary_pos_emb`` keep the reference names and arguments,
-attention.py:68-88); the paged ops, which the reference only exposes as
-``torch.ops.libdvatt.*``, get thin wrappers that allocate ``out`` when it is not given.
+"""Python wrappers in the style of python/dvattn/attention.py (``dvattn_fused``,
+``dvattn_sdpa``, ``dvattn_rope``, ``rotate_half``, ``apply_rotary_pos_emb`` keep the
+reference names and arguments, attention.py:17-88); the paged ops, which the reference
+only exposes as ``torch.ops.libdvatt.*``, get thin wrappers that allocate ``out`` when it
+is not given.
 """
 from __future__ import annotations
 
@@ -10,6 +11,31 @@ from typing import Optional
 import torch
 
 _ops = torch.ops.libdvatt
+
+
+def dvattn_fused(queries: torch.Tensor, locations: torch.Tensor, keys: list, values: list, scale: float,
+                 fragment_lengths, cosines: torch.Tensor, sines: torch.Tensor, *, rotated_queries, out):
+    """Rope + attention over contiguous per-turn fragments (attention.py:17-21): queries
+    [W,Hq,S,E] are rotated into ``rotated_queries`` [F,W,Hq,S,E], then attend."""
+    _ops.dvattn_fused(out, rotated_queries, scale, locations, queries.contiguous(), fragment_lengths, keys, values,
+                      cosines, sines)
+    return out
+
+
+def dvattn_sdpa(queries: torch.Tensor, locations: torch.Tensor, keys: list, values: list, scale: float,
+                fragment_lengths=None, out=None) -> torch.Tensor:
+    """Attention over contiguous per-turn fragments (attention.py:24-34): queries
+    [F,W,Hq,S,E] (rotated), keys/values F tensors [Hkv,L_f,E] or [B,Hkv,L_f,E] (B = 1 or W),
+    locations [F,W,S] -> out [W,Hq,S,Ev]."""
+    if out is None:
+        out = torch.empty((queries.size(1), queries.size(2), queries.size(3), values[0].size(-1)),
+                          dtype=queries.dtype, device=queries.device)
+    if fragment_lengths is None:
+        fragment_lengths = torch.tensor([k.size(-2) for k in keys], dtype=torch.int32, device=queries.device)
+    keys = [k.contiguous() for k in keys]
+    values = [v.contiguous() for v in values]
+    _ops.dvattn_sdpa(out, scale, locations, queries.contiguous(), fragment_lengths, keys, values)
+    return out
 
 
 def dvattn_paged_sdpa(queries: torch.Tensor, locations: torch.Tensor, cosines: torch.Tensor, sines: torch.Tensor,

@@ -48,6 +48,8 @@ EXPORTS = [
     "dvattn_rope",
     "dvattn_varlen_rope",
     "dvattn_lse_merge",
+    "dvattn_sdpa_workspace_size",
+    "dvattn_sdpa",
 ]
 
 _vp = ctypes.c_void_p
@@ -71,6 +73,14 @@ class VarlenArgs(ctypes.Structure):
                 ("out_f32", _vp)]
 
 
+class SdpaArgs(ctypes.Structure):
+    _fields_ = [("dtype", _i), ("F", _i), ("W", _i), ("Hq", _i), ("Hkv", _i), ("E", _i), ("Ev", _i), ("S", _i),
+                ("scale", ctypes.c_float), ("out", _vp), ("queries", _vp), ("locations", _vp),
+                ("fragment_lengths", _vp), ("key_fragments", ctypes.POINTER(_vp)),
+                ("value_fragments", ctypes.POINTER(_vp)), ("fragment_rows", ctypes.POINTER(_i)),
+                ("fragment_batch", ctypes.POINTER(_i)), ("lse_out", _vp), ("out_f32", _vp)]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -90,6 +100,10 @@ def lib() -> ctypes.CDLL:
         L.dvattn_paged_sdpa.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _vp]
         L.dvattn_paged_sdpa_phase.restype = _i
         L.dvattn_paged_sdpa_phase.argtypes = [ctypes.POINTER(PagedArgs), _vp, ctypes.c_size_t, _i, _vp]
+        L.dvattn_sdpa_workspace_size.restype = ctypes.c_size_t
+        L.dvattn_sdpa_workspace_size.argtypes = [ctypes.POINTER(SdpaArgs)]
+        L.dvattn_sdpa.restype = _i
+        L.dvattn_sdpa.argtypes = [ctypes.POINTER(SdpaArgs), _vp, ctypes.c_size_t, _vp]
         L.dvattn_varlen_paged_sdpa_phase.restype = _i
         L.dvattn_varlen_paged_sdpa_phase.argtypes = [ctypes.POINTER(VarlenArgs), _vp, ctypes.c_size_t, _i, _vp]
         L.dvattn_paged_sdpa_noalloc_max_workspace.restype = ctypes.c_size_t
@@ -261,4 +275,28 @@ def lse_merge(part_out, part_lse, out, lse_out=None):
                                 out.data_ptr(), _ptr(lse_out), _stream(None))
     if st != DVATTN_OK:
         raise DvattnError(st, "dvattn_lse_merge")
+    return out
+
+
+def sdpa(out, scale, locations, queries, fragment_lengths, keys, values, lse=None, out_f32=None):
+    """dvattn_sdpa through the C ABI: queries [F,W,Hq,S,E] (rotated), keys/values lists of F
+    tensors [Hkv,L,E] or [B,Hkv,L,E] (B = 1 or W)."""
+    W, Hq, S, Ev = out.shape
+    F, E = locations.size(0), queries.size(4)
+    batched = keys[0].dim() == 4
+    fo = 1 if batched else 0
+    kp = (_vp * F)(*[k.data_ptr() for k in keys])
+    vp = (_vp * F)(*[v.data_ptr() for v in values])
+    rows = (_i * F)(*[k.size(fo + 1) for k in keys])
+    batch = (_i * F)(*[(k.size(0) if batched else 1) for k in keys])
+    a = SdpaArgs(_DTYPE.get(out.dtype, -1), F, W, Hq, keys[0].size(fo), E, Ev, S, float(scale), out.data_ptr(),
+                 queries.data_ptr(), locations.data_ptr(), fragment_lengths.data_ptr(), kp, vp, rows, batch,
+                 lse.data_ptr() if lse is not None else None, out_f32.data_ptr() if out_f32 is not None else None)
+    n = lib().dvattn_sdpa_workspace_size(ctypes.byref(a))
+    if n == 0 and W * S > 0 and Hq > 0:
+        raise DvattnError(lib().dvattn_sdpa(ctypes.byref(a), None, 0, None), "dvattn_sdpa workspace size")
+    ws = torch.empty(max(n, 256), dtype=torch.uint8, device=out.device)
+    st = lib().dvattn_sdpa(ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_sdpa")
     return out

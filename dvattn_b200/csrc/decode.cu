@@ -15,6 +15,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <vector>
 
 namespace dvb {
 
@@ -65,7 +66,7 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
     };
     auto qrow_of = [&](int row) {
         const int hq = (h0 + (row >> 4)) * p.gqa + (row & 15);
-        return static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+        return static_cast<const T*>(p.q) + (size_t)f * p.q_turn_stride + (((size_t)w * p.Hq + hq) * p.S + s) * E;
     };
     if ((hp & 7) == 0 && ((reinterpret_cast<uintptr_t>(cr) | reinterpret_cast<uintptr_t>(sr)) & 15) == 0) {
         const int npair = hp >> 3, npass = (E - R) >> 3;
@@ -271,7 +272,9 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
 
     // ---- producer: issue one tile of K and V rows into stage `st` ----
     auto issue = [&](const TileDesc& d, int st) {
-        const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+        const int* btw = p.nfrag ? nullptr : p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+        FragDesc fd{};
+        if (p.nfrag) fd = p.frag[d.f];
         const uint32_t kd = sK0 + st * C::STAGE_BYTES, vd = sV0 + st * C::STAGE_BYTES;
 #pragma unroll
         for (int i = 0; i < TILE * CPR / NT; ++i) {
@@ -282,12 +285,23 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
             int bytes = 0;
             if (r < d.n) {
                 const int pos = d.pos0 + r;
-                const int page = __ldg(btw + pos / p.BS);
-                if (p.NB <= 0 || (page >= 0 && page < p.NB)) {
-                    const size_t row = ((size_t)page * p.BS + pos % p.BS) * p.Hkv + d.hkv;
-                    ks = kc + row * E + ch * 8;
-                    vs = vc + row * E + ch * 8;
-                    bytes = 16;
+                if (p.nfrag) {  // contiguous fragment of turn d.f
+                    const int l = pos - d.off;
+                    if (l < fd.rows) {
+                        const size_t row =
+                            ((size_t)(d.ws / p.S) * fd.wmul * p.Hkv + d.hkv) * (size_t)fd.rows + (size_t)l;
+                        ks = static_cast<const T*>(fd.k) + row * E + ch * 8;
+                        vs = static_cast<const T*>(fd.v) + row * E + ch * 8;
+                        bytes = 16;
+                    }
+                } else {
+                    const int page = __ldg(btw + pos / p.BS);
+                    if (p.NB <= 0 || (page >= 0 && page < p.NB)) {
+                        const size_t row = ((size_t)page * p.BS + pos % p.BS) * p.Hkv + d.hkv;
+                        ks = kc + row * E + ch * 8;
+                        vs = vc + row * E + ch * 8;
+                        bytes = 16;
+                    }
                 }
             }
             cp_async16_zfill(kd + swz(r, ch, ROWB), ks, bytes);
@@ -331,7 +345,8 @@ __global__ void __launch_bounds__(WARPS * 32) decode_tc_kernel(PagedParams p) {
                 uint32_t pk[4] = {0u, 0u, 0u, 0u};
                 if (g < p.gqa) {
                     const int hq = d.hkv * p.gqa + g;
-                    const T* qrow = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+                    const T* qrow = static_cast<const T*>(p.q) + (size_t)d.f * p.q_turn_stride +
+                                    (((size_t)w * p.Hq + hq) * p.S + s) * E;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const int e = ch * 8 + 2 * j;
@@ -1459,7 +1474,9 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
     const float* __restrict__ vc = static_cast<const float*>(p.v);
 
     auto issue = [&](const TileDesc& d, int st) {
-        const int* btw = p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+        const int* btw = p.nfrag ? nullptr : p.bt + (size_t)row_block_table(p, d.ws) * p.maxb;
+        FragDesc fd{};
+        if (p.nfrag) fd = p.frag[d.f];
         float* kd = sK + st * C::STAGE_F;
         float* vd = sV + st * C::STAGE_F;
 #pragma unroll
@@ -1471,12 +1488,23 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
             int bytes = 0;
             if (r < d.n) {
                 const int pos = d.pos0 + r;
-                const int page = __ldg(btw + pos / p.BS);
-                if (p.NB <= 0 || (page >= 0 && page < p.NB)) {
-                    const size_t row = ((size_t)page * p.BS + pos % p.BS) * p.Hkv + d.hkv;
-                    ks = kc + row * E + ch * 4;
-                    vs = vc + row * E + ch * 4;
-                    bytes = 16;
+                if (p.nfrag) {  // contiguous fragment of turn d.f
+                    const int l = pos - d.off;
+                    if (l < fd.rows) {
+                        const size_t row =
+                            ((size_t)(d.ws / p.S) * fd.wmul * p.Hkv + d.hkv) * (size_t)fd.rows + (size_t)l;
+                        ks = static_cast<const float*>(fd.k) + row * E + ch * 4;
+                        vs = static_cast<const float*>(fd.v) + row * E + ch * 4;
+                        bytes = 16;
+                    }
+                } else {
+                    const int page = __ldg(btw + pos / p.BS);
+                    if (p.NB <= 0 || (page >= 0 && page < p.NB)) {
+                        const size_t row = ((size_t)page * p.BS + pos % p.BS) * p.Hkv + d.hkv;
+                        ks = kc + row * E + ch * 4;
+                        vs = vc + row * E + ch * 4;
+                        bytes = 16;
+                    }
                 }
             }
             cp_async16_zfill(smem_u32(kd + r * LD + ch * 4), ks, bytes);
@@ -1515,7 +1543,8 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
                 const int g = idx / E, e = idx % E;
                 float x = 0.f;
                 if (g < p.gqa) {
-                    const float* qrow = static_cast<const float*>(p.q) + (((size_t)w * p.Hq + d.hkv * p.gqa + g) * p.S + s) * E;
+                    const float* qrow = static_cast<const float*>(p.q) + (size_t)d.f * p.q_turn_stride +
+                                        (((size_t)w * p.Hq + d.hkv * p.gqa + g) * p.S + s) * E;
                     x = rotated_elem(qrow, cr, sr, e, p.R);
                 }
                 sQ[g * LD + e] = x;
@@ -1895,9 +1924,9 @@ static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
 }
 
 struct DecodeLayout {
-    size_t off_P, off_rs, off_cs, off_po, off_pl, total;
+    size_t off_P, off_rs, off_cs, off_po, off_pl, off_fd, total;
 };
-static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int slot_heads) {
+static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int slot_heads, int nfrag = 0) {
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
     DecodeLayout L;
     L.off_P = 256;
@@ -1905,7 +1934,8 @@ static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int 
     L.off_cs = L.off_rs + (varlen ? up(sizeof(int) * (size_t)WS) : 0);
     L.off_po = L.off_cs + up(sizeof(long long) * (size_t)(n_launch + 1));
     L.off_pl = L.off_po + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16 * E);
-    L.total = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16);
+    L.off_fd = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16);
+    L.total = L.off_fd + up(sizeof(FragDesc) * (size_t)nfrag);
     return L;
 }
 
@@ -1928,14 +1958,16 @@ size_t decode_workspace_size(const dvattn_paged_args* a) {
 // cs_stride, cu_q/nseq); fills the workspace-derived fields.
 static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
     KernelChoice kc;
-    if (!choose(dtype, p.E, p.Hkv, p.BS, p.NB, kc)) return DVATTN_ERR_UNSUPPORTED;
+    // contiguous fragments: the cp.async kernels (per-row addresses), not the TMA ones
+    if (p.nfrag ? !pick_kernel(dtype, p.E, kc) : !choose(dtype, p.E, p.Hkv, p.BS, p.NB, kc))
+        return DVATTN_ERR_UNSUPPORTED;
     int n_launch = 0;
     int st = device_sms_and_occ(kc, n_launch);
     if (st != DVATTN_OK) return st;
     p.hsplit = kc.row ? 1 : p.Hkv;
     p.bs_shift = (p.BS & (p.BS - 1)) == 0 ? __builtin_ctz((unsigned)p.BS) : -1;
     p.slot_heads = kc.row ? p.Hkv : 1;
-    const DecodeLayout L = decode_layout(p.WS, p.E, n_launch, p.cu_q != nullptr, p.slot_heads);
+    const DecodeLayout L = decode_layout(p.WS, p.E, n_launch, p.cu_q != nullptr, p.slot_heads, p.nfrag);
     if (!workspace || wbytes < L.total || (reinterpret_cast<uintptr_t>(workspace) & 255)) return DVATTN_ERR_WORKSPACE;
     char* wsb = static_cast<char*>(workspace);
     p.sched = reinterpret_cast<DecodeSched*>(wsb);
@@ -1944,6 +1976,15 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.part_o = reinterpret_cast<float*>(wsb + L.off_po);
     p.part_lse = reinterpret_cast<float*>(wsb + L.off_pl);
     p.cstart = reinterpret_cast<long long*>(wsb + L.off_cs);
+    if (p.nfrag) {
+        // the fragment descriptors travel in the workspace (staged from the host array)
+        if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) {
+            if (cudaMemcpyAsync(wsb + L.off_fd, p.frag, sizeof(FragDesc) * (size_t)p.nfrag, cudaMemcpyHostToDevice,
+                                stream) != cudaSuccess)
+                return DVATTN_ERR_CUDA;
+        }
+        p.frag = reinterpret_cast<const FragDesc*>(wsb + L.off_fd);
+    }
     {
         // a query rotation costs about as long as streaming ~96 KB of the cache
         const int esz = dtype == DVATTN_FLOAT32 ? 4 : 2;
@@ -2120,6 +2161,68 @@ int varlen_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, c
     p.lse_out = v->lse_out; p.out_f32 = v->out_f32;
     p.cu_q = v->cu_seqlens_q; p.nseq = v->W; p.cs_stride = v->R / 2;
     return run_schedule(p, v->dtype, workspace, wbytes, stream, phase);
+}
+
+// ---------------------------------------------------------------------------------
+// Contiguous fragments (dvattn_sdpa): the paged machinery with per-turn fragment
+// addressing, per-turn rotated queries and no rotation.
+static int sdpa_validate(const dvattn_sdpa_args* a) {
+    if (!a) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->dtype < 0 || a->dtype > 2) return DVATTN_ERR_UNSUPPORTED;
+    if (a->F < 1 || a->F > 4096 || a->W < 0 || a->Hq < 0 || a->Hkv <= 0 || a->E <= 0 || a->Ev <= 0 || a->S < 0)
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->Hq % a->Hkv) return DVATTN_ERR_INVALID_ARGUMENT;
+    const int gqa = a->Hq / a->Hkv;
+    if (gqa > 16 || (a->Hq > 0 && gqa < 1)) return DVATTN_ERR_UNSUPPORTED;
+    if (a->E != a->Ev) return DVATTN_ERR_UNSUPPORTED;
+    KernelChoice kc;
+    if (!pick_kernel(a->dtype, a->E, kc)) return DVATTN_ERR_UNSUPPORTED;
+    if (!a->key_fragments || !a->value_fragments || !a->fragment_rows || !a->fragment_batch)
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    for (int f = 0; f < a->F; ++f) {
+        if (a->fragment_rows[f] < 0) return DVATTN_ERR_INVALID_ARGUMENT;
+        if (a->fragment_batch[f] != 1 && a->fragment_batch[f] != a->W) return DVATTN_ERR_INVALID_ARGUMENT;
+        if (a->fragment_rows[f] > 0 && (!a->key_fragments[f] || !a->value_fragments[f] ||
+                                        misaligned16(a->key_fragments[f]) || misaligned16(a->value_fragments[f])))
+            return DVATTN_ERR_INVALID_ARGUMENT;
+    }
+    return DVATTN_OK;
+}
+
+size_t sdpa_workspace_size(const dvattn_sdpa_args* a) {
+    if (sdpa_validate(a) != DVATTN_OK) return 0;
+    KernelChoice kc;
+    pick_kernel(a->dtype, a->E, kc);
+    int n_launch = 0;
+    if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
+    return decode_layout(a->W * a->S, a->E, n_launch, false, 1, a->F).total;
+}
+
+int sdpa_launch(const dvattn_sdpa_args* a, void* workspace, size_t wbytes, cudaStream_t stream) {
+    int st = sdpa_validate(a);
+    if (st != DVATTN_OK) return st;
+    const int WS = a->W * a->S;
+    if (WS == 0 || a->Hq == 0) return DVATTN_OK;
+    if (!a->out || !a->queries || !a->locations || !a->fragment_lengths) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (misaligned16(a->queries) || misaligned16(a->out) || (a->out_f32 && misaligned16(a->out_f32)))
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    std::vector<FragDesc> fd((size_t)a->F);
+    for (int f = 0; f < a->F; ++f)
+        fd[f] = FragDesc{a->key_fragments[f], a->value_fragments[f], a->fragment_rows[f], a->fragment_batch[f] == 1 ? 0 : 1};
+    PagedParams p{};
+    p.F = a->F; p.W = a->W; p.Hq = a->Hq; p.Hkv = a->Hkv; p.E = a->E; p.S = a->S; p.R = 0;
+    p.BS = 1; p.maxb = 0; p.WS = WS; p.gqa = a->Hq / a->Hkv;
+    p.cap = 0x7fffffff;
+    p.NB = 0;
+    p.scale_log2 = a->scale * kLog2e;
+    p.out = a->out; p.q = a->queries; p.cos = nullptr; p.sin = nullptr; p.loc = a->locations;
+    p.L = a->fragment_lengths; p.k = nullptr; p.v = nullptr; p.bt = nullptr;
+    p.lse_out = a->lse_out; p.out_f32 = a->out_f32;
+    p.cu_q = nullptr; p.nseq = 0; p.cs_stride = 0;
+    p.nfrag = a->F;
+    p.q_turn_stride = (long long)a->W * a->Hq * a->S * a->E;
+    p.frag = fd.data();  // staged into the workspace by run_schedule
+    return run_schedule(p, a->dtype, workspace, wbytes, stream, DVATTN_PHASE_ALL);
 }
 
 }  // namespace dvb

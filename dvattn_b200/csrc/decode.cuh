@@ -12,6 +12,9 @@ int decode_launch(const dvattn_paged_args* a, void* workspace, size_t wbytes, cu
 
 size_t varlen_workspace_size(const dvattn_varlen_args* a);
 int varlen_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
+// contiguous fragments (the dvattn_sdpa op)
+size_t sdpa_workspace_size(const dvattn_sdpa_args* a);
+int sdpa_launch(const dvattn_sdpa_args* a, void* workspace, size_t wbytes, cudaStream_t stream);
 // tcgen05 varlen prefill (prefill.cu): used by varlen_launch when prefill_eligible()
 bool prefill_eligible(const dvattn_varlen_args* a);
 size_t prefill_workspace_size(const dvattn_varlen_args* a);

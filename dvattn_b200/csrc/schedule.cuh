@@ -22,6 +22,16 @@
 
 namespace dvb {
 
+// One contiguous K/V fragment of the dvattn_sdpa op: K of turn f, KV head h, worker w,
+// key l at k + ((w * wmul * Hkv + h) * rows + l) * E (wmul = 0: one fragment shared by
+// all workers, 1: a batch dimension of W); keys l >= rows read as zeros.
+struct FragDesc {
+    const void* k;
+    const void* v;
+    int rows;
+    int wmul;
+};
+
 struct DecodeSched {
     long long U;  // total units
     int n_eff;    // CTAs that own units (<= n_launch)
@@ -67,6 +77,12 @@ struct PagedParams {
     // 1: no prep kernel; every attention CTA computes the split itself (cta_prefix /
     // cta_boundary) and publishes its share of P / cstart / the header for the merge
     int fused;
+    // contiguous fragments (dvattn_sdpa): nfrag = F descriptors in device memory, keys
+    // addressed per turn instead of through the block table; the queries are per turn
+    // (q_turn_stride elements apart) and already rotated (R = 0)
+    int nfrag;
+    long long q_turn_stride;
+    const FragDesc* frag;
 };
 
 
@@ -292,6 +308,7 @@ __global__ void __launch_bounds__(1024) decode_prep_kernel(PagedParams p) {
 // run their own copy in lock step.
 struct TileDesc {
     int ws, hkv, f, pos0, n;
+    int off;  // logical position of the turn's first key
     bool new_seg, new_turn, seg_last, seg_complete, first_piece;
 };
 
@@ -375,6 +392,7 @@ template <int TILE> struct TileIter {
         d.hkv = hkv;
         d.f = f;
         d.pos0 = off + t;
+        d.off = off;
         d.n = n;
         d.new_seg = pend_seg;
         d.new_turn = pend_turn;

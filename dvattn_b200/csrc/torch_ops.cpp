@@ -314,18 +314,94 @@ void dvattn_lse_merge_op(at::Tensor& out, const c10::optional<at::Tensor>& lse_o
                  "dvattn_lse_merge");
 }
 
-// The contiguous-fragment ops exist in the schema set but are not built for B200.
-void not_built(const char* name) {
-    TORCH_CHECK(false, "dvattn: ", name,
-                " (contiguous-fragment attention) is not part of the B200 build; use dvattn_paged_sdpa over a paged cache");
+// ---------------------------------------------------------------------------------
+// dvattn_sdpa / dvattn_fused: contiguous per-turn fragments (src/binding.cu:79-149,
+// 356-372).  key_fragments[f] is [Hkv, L_f, E] or [B, Hkv, L_f, E] with B = 1 (one
+// fragment shared by the W workers) or B = W; queries are [F, W, Hq, S, E], rotated.
+// ---------------------------------------------------------------------------------
+void sdpa_impl(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+               const at::Tensor& fragment_lengths, const std::vector<at::Tensor>& keys,
+               const std::vector<at::Tensor>& values, const char* name) {
+    const c10::cuda::CUDAGuard guard(out.device());
+    const int dt = dtype_code(out);
+    TORCH_CHECK(out.dim() == 4, name, ": output must be [W, Hq, S, Ev]");
+    TORCH_CHECK(queries.dim() == 5 && locations.dim() == 3 && fragment_lengths.dim() == 1, name, ": wrong tensor ranks");
+    TORCH_CHECK(queries.scalar_type() == out.scalar_type(), name, ": queries must have the output dtype");
+    check_i32(locations, "locations");
+    check_i32(fragment_lengths, "fragment_lengths");
+    check_all(out, {Named{&out, "output"}, Named{&queries, "queries"}, Named{&locations, "locations"},
+                    Named{&fragment_lengths, "fragment_lengths"}});
+    const int W = out.size(0), Hq = out.size(1), S = out.size(2), Ev = out.size(3);
+    const int F = locations.size(0), E = queries.size(4);
+    TORCH_CHECK(locations.size(1) == W && locations.size(2) == S, name, ": locations must be [F, W, S]");
+    TORCH_CHECK(queries.size(0) == F && queries.size(1) == W && queries.size(2) == Hq && queries.size(3) == S,
+                name, ": queries must be [F, W, Hq, S, E]");
+    TORCH_CHECK(fragment_lengths.size(0) == F, name, ": fragment_lengths must be [F]");
+    TORCH_CHECK((int)keys.size() == F && (int)values.size() == F, name, ": need one key and one value fragment per turn");
+    TORCH_CHECK(F > 0, name, ": at least one fragment");
+    const bool batched = keys[0].dim() == 4;
+    const int fo = batched ? 1 : 0;
+    const int Hkv = keys[0].size(fo);
+    std::vector<const void*> kp(F), vp(F);
+    std::vector<int> rows(F), batch(F);
+    for (int f = 0; f < F; ++f) {
+        const at::Tensor& k = keys[f];
+        const at::Tensor& v = values[f];
+        TORCH_CHECK(k.dim() == 3 + fo && v.dim() == 3 + fo, name, ": fragments must all be [Hkv, L, E] or all [B, Hkv, L, E]");
+        TORCH_CHECK(k.scalar_type() == out.scalar_type() && v.scalar_type() == out.scalar_type(), name,
+                    ": fragments must have the output dtype");
+        check_cuda_tensor(k, "key fragment", out);
+        check_cuda_tensor(v, "value fragment", out);
+        TORCH_CHECK(k.size(fo) == Hkv && v.size(fo) == Hkv, name, ": fragments must have Hkv heads");
+        TORCH_CHECK(v.size(fo + 1) == k.size(fo + 1), name, ": key and value fragment lengths differ");
+        TORCH_CHECK(k.size(fo + 2) == E && v.size(fo + 2) == Ev, name, ": fragment head dims must be E / Ev");
+        const int B = batched ? (int)k.size(0) : 1;
+        TORCH_CHECK(B == 1 || B == W, name, ": fragment batch must be 1 or W");
+        TORCH_CHECK(!batched || v.size(0) == B, name, ": key and value fragment batches differ");
+        kp[f] = k.const_data_ptr();
+        vp[f] = v.const_data_ptr();
+        rows[f] = (int)k.size(fo + 1);
+        batch[f] = B;
+    }
+    dvattn_sdpa_args a{};
+    a.dtype = dt;
+    a.F = F; a.W = W; a.Hq = Hq; a.Hkv = Hkv; a.E = E; a.Ev = Ev; a.S = S;
+    a.scale = static_cast<float>(scale);
+    a.out = out.data_ptr();
+    a.queries = queries.const_data_ptr();
+    a.locations = locations.const_data_ptr<int>();
+    a.fragment_lengths = fragment_lengths.const_data_ptr<int>();
+    a.key_fragments = kp.data();
+    a.value_fragments = vp.data();
+    a.fragment_rows = rows.data();
+    a.fragment_batch = batch.data();
+    int st = dvattn_sdpa(&a, nullptr, 0, cur_stream(out));  // validation only when nothing to do
+    if (st == DVATTN_ERR_WORKSPACE) {
+        const size_t wsb = dvattn_sdpa_workspace_size(&a);
+        TORCH_CHECK(wsb > 0, name, ": could not size the workspace");
+        at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
+        st = dvattn_sdpa(&a, ws.data_ptr(), wsb, cur_stream(out));
+    }
+    check_status(st, name);
 }
-void dvattn_sdpa_op(at::Tensor&, double, const at::Tensor&, const at::Tensor&, const at::Tensor&,
-                    const std::vector<at::Tensor>&, const std::vector<at::Tensor>&) {
-    not_built("dvattn_sdpa");
+
+void dvattn_sdpa_op(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                    const at::Tensor& fragment_lengths, const std::vector<at::Tensor>& keys,
+                    const std::vector<at::Tensor>& values) {
+    sdpa_impl(out, scale, locations, queries, fragment_lengths, keys, values, "dvattn_sdpa");
 }
-void dvattn_fused_op(at::Tensor&, at::Tensor&, double, const at::Tensor&, const at::Tensor&, const at::Tensor&,
-                     const std::vector<at::Tensor>&, const std::vector<at::Tensor>&, const at::Tensor&, const at::Tensor&) {
-    not_built("dvattn_fused");
+
+// rope into rq, then attention over the (made contiguous) fragments, as the reference
+void dvattn_fused_op(at::Tensor& out, at::Tensor& rq, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                     const at::Tensor& fragment_lengths, const std::vector<at::Tensor>& keys,
+                     const std::vector<at::Tensor>& values, const at::Tensor& cosines, const at::Tensor& sines) {
+    std::vector<at::Tensor> kc, vc;
+    kc.reserve(keys.size());
+    vc.reserve(values.size());
+    for (const at::Tensor& k : keys) kc.push_back(k.contiguous());
+    for (const at::Tensor& v : values) vc.push_back(v.contiguous());
+    dvattn_rope_op(rq, queries, cosines, sines);
+    sdpa_impl(out, scale, locations, rq, fragment_lengths, kc, vc, "dvattn_fused");
 }
 
 }  // namespace

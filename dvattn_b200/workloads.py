@@ -263,6 +263,79 @@ def make_varlen(turn_lens: Sequence[Sequence[int]], q_lens: Sequence[int], Hq: i
         meta=dict(W=W, F=F, T=T, Hq=Hq, Hkv=Hkv, E=E, Ev=Ev, R=R, BS=BS, seed=seed, q_lens=ql, turn_lens=tl))
 
 
+@dataclass
+class SdpaCase:
+    """Inputs of one dvattn_sdpa / dvattn_fused call over contiguous per-turn fragments.
+    ``queries`` [W,Hq,S,E] (unrotated, for dvattn_fused), ``rotated`` [F,W,Hq,S,E] (the
+    dvattn_sdpa input, rotated from queries with cos/sin), keys/values F tensors
+    [B,Hkv,L_f,E] (B = W, or 1 for fragments shared by all workers; ``batch=None`` gives
+    3-D [Hkv,L_f,E] tensors, which the reference reads as B = 1 when W = 1)."""
+    queries: torch.Tensor
+    rotated: torch.Tensor
+    cosines: torch.Tensor
+    sines: torch.Tensor
+    locations: torch.Tensor
+    fragment_lengths: torch.Tensor
+    keys: list
+    values: list
+    scale: float
+    meta: dict
+
+    @property
+    def dtype(self):
+        return self.queries.dtype
+
+    def to(self, device) -> "SdpaCase":
+        mv = lambda t: t.to(device)
+        return SdpaCase(mv(self.queries), mv(self.rotated), mv(self.cosines), mv(self.sines), mv(self.locations),
+                        mv(self.fragment_lengths), [mv(k) for k in self.keys], [mv(v) for v in self.values],
+                        self.scale, dict(self.meta))
+
+
+def make_sdpa(lens: Sequence[int], W: int, Hq: int, Hkv: int, E: int, R: int, dtype, seed: int = 0, S: int = 1,
+              batch="w", device="cpu", skip_turns: Sequence[int] = ()) -> SdpaCase:
+    """Contiguous-fragment inputs.  Turn f has L_f = lens[f] keys; the query (w, s) of turn
+    f sees keys l <= loc[f,w,s] with loc ~ U[0, L_f) (-1 for turns listed in skip_turns and
+    for empty fragments), and every query sees at least one key in some turn."""
+    F = len(lens)
+    rs = np.random.RandomState(seed)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    q = _randn((W, Hq, S, E), dtype, gen, device)
+    loc = np.full((F, W, S), -1, np.int64)
+    for f in range(F):
+        if lens[f] > 0 and f not in skip_turns:
+            loc[f] = rs.randint(0, lens[f], size=(W, S))
+    live = [f for f in range(F) if lens[f] > 0 and f not in skip_turns]
+    assert live, "at least one visible turn"
+    dead = (loc.max(axis=0) < 0)
+    loc[live[0]][dead] = lens[live[0]] - 1
+    pos = rs.randint(0, 4096, size=(F, W, S))
+    cos, sin = rope_angles(torch.from_numpy(pos).to(device), R)
+    B = W if batch == "w" else 1
+    keys, vals = [], []
+    for f in range(F):
+        shape = (B, Hkv, lens[f], E) if batch is not None else (Hkv, lens[f], E)
+        keys.append(_randn(shape, dtype, gen, device))
+        vals.append(_randn(shape, dtype, gen, device))
+    # rotated queries as the reference's apply_rotary_pos_emb (first R entries rotated)
+    rq = []
+    for f in range(F):
+        if R == 0:
+            rq.append(q.clone())
+            continue
+        c = cos[f][:, None].to(torch.float32)   # [W,1,S,R]
+        sn = sin[f][:, None].to(torch.float32)
+        xr = q[..., :R].to(torch.float32)
+        rot = torch.cat((-xr[..., R // 2:], xr[..., :R // 2]), -1)
+        rq.append(torch.cat(((xr * c + rot * sn).to(dtype), q[..., R:]), -1))
+    return SdpaCase(queries=q, rotated=torch.stack(rq).contiguous(), cosines=cos, sines=sin,
+                    locations=torch.from_numpy(loc.astype(np.int32)).to(device),
+                    fragment_lengths=torch.tensor(list(lens), dtype=torch.int32, device=device),
+                    keys=keys, values=vals, scale=1.0 / math.sqrt(E),
+                    meta=dict(F=F, W=W, Hq=Hq, Hkv=Hkv, E=E, R=R, S=S, batch=batch, seed=seed))
+
+
 def varlen_flops(case: VarlenCase) -> int:
     Hq = case.queries.size(1)
     E, Ev = case.queries.size(2), case.v_cache.size(3)

@@ -96,6 +96,29 @@ typedef struct dvattn_varlen_args {
     float* out_f32;               /* optional [T,Hq,Ev] f32 copy of the output          */
 } dvattn_varlen_args;
 
+/*
+ * Arguments of one contiguous-fragment call, the `dvattn_sdpa` schema
+ * (src/binding.cu:79-149, 410-411): already rotated per-turn queries and one K and one V
+ * tensor per turn ("fragment"), each [B_f, Hkv, rows_f, E] with B_f = 1 (shared by all W
+ * workers) or W.  Key l of turn f is visible to (w, s) iff l <= locations[f,w,s],
+ * l < fragment_lengths[f] and l < rows_f.
+ */
+typedef struct dvattn_sdpa_args {
+    int dtype;
+    int F, W, Hq, Hkv, E, Ev, S;
+    float scale;
+    void* out;                          /* [W,Hq,S,Ev] T                                   */
+    const void* queries;                /* [F,W,Hq,S,E] T, rotated                         */
+    const int* locations;               /* [F,W,S] i32 (device)                            */
+    const int* fragment_lengths;        /* [F] i32 (device)                                */
+    const void* const* key_fragments;   /* host array of F device pointers                 */
+    const void* const* value_fragments; /* host array of F device pointers                 */
+    const int* fragment_rows;           /* host array [F]: rows_f                          */
+    const int* fragment_batch;          /* host array [F]: B_f (1 or W)                    */
+    float* lse_out;                     /* optional [W,Hq,S] natural-log LSE               */
+    float* out_f32;                     /* optional [W,Hq,S,Ev] f32 copy of the output     */
+} dvattn_sdpa_args;
+
 /* ABI version of this header (bumped on any layout change of the structs above). */
 int dvattn_abi_version(void);
 
@@ -172,6 +195,18 @@ int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace,
  */
 int dvattn_varlen_paged_sdpa_phase(const dvattn_varlen_args* args, void* workspace,
                                    size_t workspace_bytes, int phase, dvattn_stream_t stream);
+
+/* Workspace bytes of dvattn_sdpa (0 on invalid arguments). */
+size_t dvattn_sdpa_workspace_size(const dvattn_sdpa_args* args);
+
+/*
+ * Attention over contiguous per-turn K/V fragments: the `dvattn_sdpa` op
+ * (`dvattn_attention_tpl` + `v21::dvattn_attention_gpu`, src/binding.cu:79-149,
+ * src/kernels/kernel_v21.cuh:17-431).  The fragment descriptors are copied to the
+ * workspace with one host-to-device copy on `stream`.  `dvattn_fused`
+ * (src/binding.cu:356-372) is dvattn_rope into the rotated-query buffer followed by this.
+ */
+int dvattn_sdpa(const dvattn_sdpa_args* args, void* workspace, size_t workspace_bytes, dvattn_stream_t stream);
 
 /*
  * Standalone query rotation, schema `dvattn_rope` (src/binding.cu:41-77, src/rope.cuh:2-65):

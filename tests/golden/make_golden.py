@@ -131,9 +131,33 @@ def golden_varlen(ref, name, case: wl.VarlenCase):
     print("wrote", name, tuple(out.shape))
 
 
+def golden_sdpa(ref, name, case: wl.SdpaCase):
+    """Contiguous fragments: dvattn_sdpa_pt on the case's fragments directly, and the
+    rotated queries of dvattn_fused with apply_rotary_pos_emb."""
+    q, loc, cos, sin = case.queries, case.locations, case.cosines, case.sines
+    F = loc.shape[0]
+    if cos.shape[-1]:
+        rq = torch.stack([ref.apply_rotary_pos_emb(q, cos[f], sin[f], unsqueeze_dim=1) for f in range(F)])
+    else:
+        rq = torch.stack([q.clone() for _ in range(F)])
+    res, qk, _ = ref.dvattn_sdpa_pt(rq, loc, case.keys, case.values, case.scale, return_intermediate_results=True)
+    lse = torch.logsumexp(case.scale * qk, dim=-1)
+    assert torch.isfinite(res).all(), name
+    t = dict(queries=q, rotated=rq, cosines=cos, sines=sin, locations=loc, fragment_lengths=case.fragment_lengths,
+             out=res.to(q.dtype), out_f32=res, lse=lse)
+    for f in range(F):
+        t["key_%d" % f] = case.keys[f]
+        t["value_%d" % f] = case.values[f]
+    fixtures.save(name, t, dict(kind="sdpa", scale=case.scale, F=F))
+    print("wrote", name, tuple(res.shape))
+
+
 def main():
     ref = load_reference()
     bf, hf, f32 = torch.bfloat16, torch.float16, torch.float32
+    only = sys.argv[1:]  # optional: kinds to (re)generate, e.g. "sdpa"
+    if only and "paged" not in only and "varlen" not in only:
+        return sdpa_only(ref)
     golden_paged(ref, "paged_f32_config1", wl.config1())
     golden_paged(ref, "paged_bf16_2turn", wl.make_paged([[37, 90], [150, 3], [64, 64]], Hq=32, Hkv=2, E=128, R=64,
                                                         BS=16, dtype=bf, seed=11))
@@ -151,6 +175,24 @@ def main():
                                                           R=64, BS=16, dtype=hf, seed=22))
     golden_varlen(ref, "varlen_f32", wl.make_varlen([[6], [50]], [6, 2], Hq=16, Hkv=1, E=128, R=128, BS=16,
                                                     dtype=f32, seed=23))
+    golden_sdpa(ref, "sdpa_bf16_w4", wl.make_sdpa([37, 90], W=4, Hq=32, Hkv=2, E=128, R=64, dtype=bf, seed=31))
+    golden_sdpa(ref, "sdpa_f16_e256_shared_s2", wl.make_sdpa([20, 5, 61], W=3, Hq=16, Hkv=1, E=256, R=64, dtype=hf,
+                                                              seed=32, S=2, batch=1))
+    golden_sdpa(ref, "sdpa_f32_e64_3d", wl.make_sdpa([33, 12], W=1, Hq=16, Hkv=2, E=64, R=32, dtype=f32, seed=33,
+                                                      batch=None))
+    golden_sdpa(ref, "sdpa_bf16_gqa4_skip", wl.make_sdpa([50, 0, 70], W=2, Hq=16, Hkv=4, E=128, R=0, dtype=bf,
+                                                          seed=34, skip_turns=(0,)))
+
+
+def sdpa_only(ref):
+    bf, hf, f32 = torch.bfloat16, torch.float16, torch.float32
+    golden_sdpa(ref, "sdpa_bf16_w4", wl.make_sdpa([37, 90], W=4, Hq=32, Hkv=2, E=128, R=64, dtype=bf, seed=31))
+    golden_sdpa(ref, "sdpa_f16_e256_shared_s2", wl.make_sdpa([20, 5, 61], W=3, Hq=16, Hkv=1, E=256, R=64, dtype=hf,
+                                                              seed=32, S=2, batch=1))
+    golden_sdpa(ref, "sdpa_f32_e64_3d", wl.make_sdpa([33, 12], W=1, Hq=16, Hkv=2, E=64, R=32, dtype=f32, seed=33,
+                                                      batch=None))
+    golden_sdpa(ref, "sdpa_bf16_gqa4_skip", wl.make_sdpa([50, 0, 70], W=2, Hq=16, Hkv=4, E=128, R=0, dtype=bf,
+                                                          seed=34, skip_turns=(0,)))
 
 
 if __name__ == "__main__":
