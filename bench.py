@@ -34,6 +34,7 @@ import sys
 import threading
 import time
 
+import numpy as np
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -564,6 +565,200 @@ def run_varlen(args, world, rank, local):
             "cpu_baseline": cpu}), flush=True)
 
 
+def run_sdpa(args, world, rank, local):
+    """Config 2's shape on the contiguous-fragment op dvattn_sdpa (row f-1): one K and one V
+    fragment per turn [W, Hkv, L_f, E], each worker attending its own keys.  Same legs as
+    run_ours: value over the C ABI with three rotating fragment sets, e2e through
+    torch.ops.libdvatt.dvattn_sdpa with the per-turn queries and locations copied from
+    pinned host memory and the output copied back."""
+    import dvattn_b200  # registers torch.ops.libdvatt
+    from dvattn_b200 import capi
+    from dvattn_b200 import workloads as wl
+    from oracle import dvattn_oracle as O  # CPU baseline leg only
+    dev = f"cuda:{local}"
+    hbm_peak, _, peak_kind = load_peaks()
+    case = wl.config2_sdpa(device=dev)
+    nbytes = wl.sdpa_bytes(case)
+    sets = [(case.keys, case.values)]
+    for _ in range(2):
+        sets.append(([torch.randn_like(k, dtype=torch.float32).to(k.dtype) for k in case.keys],
+                     [torch.randn_like(v, dtype=torch.float32).to(v.dtype) for v in case.values]))
+    W, Hq, S, E = case.queries.shape
+    out = torch.empty((W, Hq, S, E), dtype=case.dtype, device=dev)
+
+    def step(i):
+        ks, vs = sets[i % 3]
+        capi.sdpa(out, case.scale, case.locations, case.rotated, case.fragment_lengths, ks, vs)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.begin()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.end()
+    clocks = sampler.stop() if sampler else None
+    barrier(world)
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+
+    host_in = [t.cpu().pin_memory() for t in (case.rotated, case.locations)]
+    dev_in = [torch.empty_like(t, device=dev) for t in host_in]
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step(i):
+        for h, d in zip(host_in, dev_in):
+            d.copy_(h, non_blocking=True)
+        rq, loc = dev_in
+        ks, vs = sets[i % 3]
+        torch.ops.libdvatt.dvattn_sdpa(out, case.scale, loc, rq, case.fragment_lengths, ks, vs)
+        host_out.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    total = sum_over_ranks(float(nbytes), world)
+    value = total / (t_ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = len(os.sched_getaffinity(0))
+        torch.set_num_threads(threads)
+        n = 2
+        keys = [k[:n].cpu() for k in case.keys]
+        vals = [v[:n].cpu() for v in case.values]
+        rq, loc = case.rotated[:, :n].cpu(), case.locations[:, :n].cpu()
+        O.sdpa_pt(rq, loc, keys, vals, case.scale)
+        t0 = time.perf_counter()
+        O.sdpa_pt(rq, loc, keys, vals, case.scale)
+        dt = time.perf_counter() - t0
+        sub = wl.SdpaCase(case.queries[:n], rq, case.cosines[:, :n], case.sines[:, :n], loc, case.fragment_lengths.cpu(),
+                          keys, vals, case.scale, {})
+        cpu = {"value": round(wl.sdpa_bytes(sub) / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": "first 2 of the 32 workers (reference dvattn_sdpa_pt restated, padded fragments)"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "contiguous-fragment attention (dvattn_sdpa) HBM GB/s", "value": round(value, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bfloat16", "data": "synthetic (seeded N(0,1) q/k/v, config-2 lengths)",
+            "config": {"workload": "sdpa2: config 2 on dvattn_sdpa, 2 turns of fragments [32, 4, L_f, 128] bf16, "
+                                   "64 query heads", "bytes_per_step_per_gpu": nbytes,
+                       "parallelism": f"batch-replica x{world}", "l2": "3 rotating fragment sets (~2 GB each)"},
+            "roofline": {"bound": "hbm", "kernel": "decode_tc_kernel (fragment addressing) + merge",
+                         "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                         "timing": "whole call (schedule + attention + merge), back to back", "traffic": None},
+            "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_ms * 1e3, 2),
+                    "api": "torch.ops.libdvatt.dvattn_sdpa"},
+            "gpu_launches": 3 * args.steps, "clocks": clocks, "cpu_baseline": cpu}), flush=True)
+
+
+def run_append(args, world, rank, local):
+    """Paged KV append with fused K rotation (row f-3) on config 4's prefill shape: 16
+    workers, n = 2048 padded new tokens, counts ~ U[1, 2048] (left padding), 2 KV heads,
+    E = 128, R = 32, page 16, bf16.  Metric: algorithmic HBM GB/s = new K/V rows read +
+    written + their cos/sin rows read."""
+    import dvattn_b200  # registers torch.ops.libdvatt
+    from dvattn_b200 import workloads as wl
+    dev = f"cuda:{local}"
+    hbm_peak, _, peak_kind = load_peaks()
+    rs = np.random.RandomState(4)
+    W, Hkv, n, E, R, BS = 16, 2, 2048, 128, 32, 16
+    counts = rs.randint(1, n + 1, size=W).astype(np.int32)
+    start = rs.randint(0, 16385, size=W).astype(np.int32)
+    maxb = (16384 + n + BS - 1) // BS
+    NB = W * maxb
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    kc = torch.zeros((NB, BS, Hkv, E), dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    bt = torch.from_numpy(rs.permutation(NB).reshape(W, maxb).astype(np.int32)).to(dev)
+    sets = []
+    for _ in range(3):
+        sets.append((torch.randn((W, Hkv, n, E), generator=g, device=dev).to(torch.bfloat16),
+                     torch.randn((W, Hkv, n, E), generator=g, device=dev).to(torch.bfloat16)))
+    cos, sin = wl.rope_angles(torch.from_numpy(rs.randint(0, 18000, (W, n))).to(dev), R)
+    pos, cnt = torch.from_numpy(start).to(dev), torch.from_numpy(counts).to(dev)
+    new = int(counts.sum())
+    nbytes = new * Hkv * 2 * E * 2 * 2 + new * R * 4 * 2 + W * 8
+
+    def step(i):
+        k, v = sets[i % 3]
+        torch.ops.libdvatt.dvattn_paged_append(kc, vc, k, v, cos, sin, bt, pos, cnt)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.begin()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.end()
+    clocks = sampler.stop() if sampler else None
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    host = [t.cpu().pin_memory() for t in sets[0]]
+    dk, dvv = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1])
+    e0.record()
+    for i in range(args.steps):
+        dk.copy_(host[0], non_blocking=True)
+        dvv.copy_(host[1], non_blocking=True)
+        torch.ops.libdvatt.dvattn_paged_append(kc, vc, dk, dvv, cos, sin, bt, pos, cnt)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    total = sum_over_ranks(float(nbytes), world)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "paged KV append with K rotation HBM GB/s", "value": round(total / (t_ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bfloat16", "data": "synthetic (seeded)",
+            "config": {"workload": "append4: 16 workers x U[1,2048] new tokens (padded to 2048), 2/128 KV heads, "
+                                   "R=32, page 16", "bytes_per_step_per_gpu": nbytes,
+                       "parallelism": f"batch-replica x{world}", "l2": "3 rotating new-token sets (34 MB each); the cache (2.3 GB) is written once per step"},
+            "roofline": {"bound": "hbm", "kernel": "paged_append_kernel",
+                         "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4), "traffic": None},
+            "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host), "d2h_bytes_per_step": 0,
+                    "us_per_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_paged_append"},
+            "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": None}), flush=True)
+
+
 def run_long3(args, world, rank, local):
     """Config 3 with its KV split across the ranks (page-aligned chunks) and the partial
     outputs merged over NCCL (all-gather of f32 O + LSE, then the LSE-merge kernel)."""
@@ -613,7 +808,8 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config2", choices=["config1", "config2", "config3", "config4", "config5", "long3"])
+    ap.add_argument("--workload", default="config2",
+                    choices=["config1", "config2", "config3", "config4", "config5", "long3", "sdpa2", "append4"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-cuda", action="store_true", help="reference arm: skip timing the reference CUDA op")
     args = ap.parse_args()
@@ -627,6 +823,10 @@ def main():
         run_long3(args, world, rank, local)
     elif args.workload == "config4":
         run_varlen(args, world, rank, local)
+    elif args.workload == "sdpa2":
+        run_sdpa(args, world, rank, local)
+    elif args.workload == "append4":
+        run_append(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
     if world > 1:

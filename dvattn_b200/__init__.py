@@ -32,6 +32,7 @@ from .api import (  # noqa: E402
     apply_rotary_pos_emb,
     dvattn_fused,
     dvattn_lse_merge,
+    dvattn_paged_append,
     dvattn_paged_sdpa,
     dvattn_rope,
     dvattn_sdpa,
@@ -44,6 +45,7 @@ __all__ = [
     "apply_rotary_pos_emb",
     "dvattn_fused",
     "dvattn_lse_merge",
+    "dvattn_paged_append",
     "dvattn_paged_sdpa",
     "dvattn_rope",
     "dvattn_sdpa",

@@ -80,6 +80,16 @@ def dvattn_varlen_paged_sdpa(queries: torch.Tensor, locations: torch.Tensor, cos
     return out
 
 
+def dvattn_paged_append(k_cache: torch.Tensor, v_cache: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                        cosines: torch.Tensor, sines: torch.Tensor, block_tables: torch.Tensor,
+                        positions: torch.Tensor, counts: Optional[torch.Tensor] = None) -> None:
+    """Append new tokens to the paged cache with the keys rotated as apply_rotary_pos_emb
+    (attention.py:302-304): keys/values [W,Hkv,n,E|Ev] (unrotated), cos/sin [W,n,R] f32
+    (full width), positions [W] i32 = logical position of worker w's first new token,
+    counts [W] i32 = how many of the n tokens are new (the last ones; left padding)."""
+    _ops.dvattn_paged_append(k_cache, v_cache, keys, values, cosines, sines, block_tables, positions, counts)
+
+
 def dvattn_rope(queries: torch.Tensor, cosines: torch.Tensor, sines: torch.Tensor, out=None) -> torch.Tensor:
     """Same signature as python/dvattn/attention.py:68-72: out [F,W,Hq,S,E]."""
     if out is None:

@@ -50,6 +50,7 @@ EXPORTS = [
     "dvattn_lse_merge",
     "dvattn_sdpa_workspace_size",
     "dvattn_sdpa",
+    "dvattn_paged_append",
 ]
 
 _vp = ctypes.c_void_p

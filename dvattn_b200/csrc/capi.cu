@@ -35,6 +35,10 @@ int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace, si
     return dvb::varlen_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), DVATTN_PHASE_ALL);
 }
 
+int dvattn_paged_append(const dvattn_append_args* args, dvattn_stream_t stream) {
+    return dvb::paged_append_launch(args, reinterpret_cast<cudaStream_t>(stream));
+}
+
 size_t dvattn_sdpa_workspace_size(const dvattn_sdpa_args* args) { return dvb::sdpa_workspace_size(args); }
 
 int dvattn_sdpa(const dvattn_sdpa_args* args, void* workspace, size_t workspace_bytes, dvattn_stream_t stream) {

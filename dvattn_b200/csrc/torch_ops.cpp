@@ -315,6 +315,59 @@ void dvattn_lse_merge_op(at::Tensor& out, const c10::optional<at::Tensor>& lse_o
 }
 
 // ---------------------------------------------------------------------------------
+// dvattn_paged_append (B200 addition): the new tokens' keys rotated as
+// apply_rotary_pos_emb and written with their values into the workers' pages
+// ---------------------------------------------------------------------------------
+void dvattn_paged_append_op(at::Tensor& k_cache, at::Tensor& v_cache, const at::Tensor& keys, const at::Tensor& values,
+                            const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& block_tables,
+                            const at::Tensor& positions, const c10::optional<at::Tensor>& counts) {
+    const c10::cuda::CUDAGuard guard(k_cache.device());
+    const int dt = dtype_code(k_cache);
+    TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4 && keys.dim() == 4 && values.dim() == 4 &&
+                    cosines.dim() == 3 && sines.dim() == 3 && block_tables.dim() == 2 && positions.dim() == 1,
+                "dvattn_paged_append: wrong tensor ranks");
+    for (const at::Tensor* t : {(const at::Tensor*)&v_cache, &keys, &values})
+        TORCH_CHECK(t->scalar_type() == k_cache.scalar_type(), "dvattn_paged_append: caches and new tokens must share the dtype");
+    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat,
+                "dvattn_paged_append: cosines/sines must be float32");
+    check_i32(block_tables, "block_tables");
+    check_i32(positions, "positions");
+    check_all(k_cache, {Named{&k_cache, "k_cache"}, Named{&v_cache, "v_cache"}, Named{&keys, "keys"},
+                        Named{&values, "values"}, Named{&cosines, "cosines"}, Named{&sines, "sines"},
+                        Named{&block_tables, "block_tables"}, Named{&positions, "positions"}});
+    const int W = keys.size(0), Hkv = keys.size(1), n = keys.size(2), E = keys.size(3);
+    const int Ev = values.size(3), R = cosines.size(2);
+    TORCH_CHECK(values.size(0) == W && values.size(1) == Hkv && values.size(2) == n, "dvattn_paged_append: values must be [W, Hkv, n, Ev]");
+    TORCH_CHECK(k_cache.size(2) == Hkv && k_cache.size(3) == E, "dvattn_paged_append: k_cache must be [NB, BS, Hkv, E]");
+    TORCH_CHECK(v_cache.size(0) == k_cache.size(0) && v_cache.size(1) == k_cache.size(1) && v_cache.size(2) == Hkv &&
+                    v_cache.size(3) == Ev, "dvattn_paged_append: v_cache must be [NB, BS, Hkv, Ev]");
+    TORCH_CHECK(cosines.size(0) == W && cosines.size(1) == n && sines.sizes() == cosines.sizes(),
+                "dvattn_paged_append: cosines/sines must be [W, n, R]");
+    TORCH_CHECK(block_tables.size(0) == W && positions.size(0) == W, "dvattn_paged_append: block_tables [W, max_blocks], positions [W]");
+    dvattn_append_args a{};
+    a.dtype = dt;
+    a.W = W; a.Hkv = Hkv; a.E = E; a.Ev = Ev; a.n = n; a.R = R;
+    a.block_size = k_cache.size(1);
+    a.max_blocks_per_seq = block_tables.size(1);
+    a.num_blocks = k_cache.size(0);
+    a.k_cache = k_cache.data_ptr();
+    a.v_cache = v_cache.data_ptr();
+    a.keys = keys.const_data_ptr();
+    a.values = values.const_data_ptr();
+    a.cosines = cosines.const_data_ptr<float>();
+    a.sines = sines.const_data_ptr<float>();
+    a.block_tables = block_tables.const_data_ptr<int>();
+    a.positions = positions.const_data_ptr<int>();
+    if (counts.has_value()) {
+        check_cuda_tensor(*counts, "counts", k_cache);
+        check_i32(*counts, "counts");
+        TORCH_CHECK(counts->numel() == W, "dvattn_paged_append: counts must be [W]");
+        a.counts = counts->const_data_ptr<int>();
+    }
+    check_status(dvattn_paged_append(&a, cur_stream(k_cache)), "dvattn_paged_append");
+}
+
+// ---------------------------------------------------------------------------------
 // dvattn_sdpa / dvattn_fused: contiguous per-turn fragments (src/binding.cu:79-149,
 // 356-372).  key_fragments[f] is [Hkv, L_f, E] or [B, Hkv, L_f, E] with B = 1 (one
 // fragment shared by the W workers) or B = W; queries are [F, W, Hq, S, E], rotated.
@@ -427,6 +480,8 @@ TORCH_LIBRARY(libdvatt, m) {
           "Tensor locations, Tensor queries, Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, "
           "Tensor v_cache, Tensor block_tables, Tensor cu_seqlens_q, Tensor cu_seqlens_k) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
     m.def("dvattn_lse_merge(Tensor(a!) output, Tensor(b!)? lse_out, Tensor part_out, Tensor part_lse) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_paged_append(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor keys, Tensor values, Tensor cosines, "
+          "Tensor sines, Tensor block_tables, Tensor positions, Tensor? counts) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
 }
 
 TORCH_LIBRARY_IMPL(libdvatt, CUDA, m) {
@@ -439,4 +494,5 @@ TORCH_LIBRARY_IMPL(libdvatt, CUDA, m) {
     m.impl("dvattn_paged_sdpa_ex", dvattn_paged_sdpa_ex_op);
     m.impl("dvattn_varlen_paged_sdpa_ex", dvattn_varlen_paged_sdpa_ex_op);
     m.impl("dvattn_lse_merge", dvattn_lse_merge_op);
+    m.impl("dvattn_paged_append", dvattn_paged_append_op);
 }

@@ -380,6 +380,41 @@ def config2(device="cpu", seed: int = 2, W: int = 32) -> PagedCase:
                       device=device)
 
 
+def config2_sdpa(device="cpu", seed: int = 2, W: int = 32) -> SdpaCase:
+    """Config 2's shape on the contiguous-fragment op: per turn one K and one V fragment
+    [W, 4, L_f, 128] bf16 with L_f the longest turn of the batch; worker w sees its own
+    len_{w,f} keys (loc = len - 1); queries per turn [2, 32, 64, 1, 128]."""
+    tl = np.asarray(config2_lengths(seed, W), dtype=np.int64)  # [W, F]
+    F = tl.shape[1]
+    Lf = tl.max(axis=0)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    Hq, Hkv, E = 64, 4, 128
+    q = _randn((W, Hq, 1, E), torch.bfloat16, gen, device)
+    rq = _randn((F, W, Hq, 1, E), torch.bfloat16, gen, device)
+    keys = [_randn((W, Hkv, int(Lf[f]), E), torch.bfloat16, gen, device) for f in range(F)]
+    vals = [_randn((W, Hkv, int(Lf[f]), E), torch.bfloat16, gen, device) for f in range(F)]
+    loc = torch.from_numpy((tl.T - 1).astype(np.int32)).reshape(F, W, 1).to(device)
+    z = torch.zeros((F, W, 1, 0), dtype=torch.float32, device=device)
+    return SdpaCase(queries=q, rotated=rq, cosines=z, sines=z.clone(), locations=loc,
+                    fragment_lengths=torch.from_numpy(Lf.astype(np.int32)).to(device), keys=keys, values=vals,
+                    scale=1.0 / math.sqrt(E), meta=dict(F=F, W=W, Hq=Hq, Hkv=Hkv, E=E, R=0, S=1, batch="w", seed=seed,
+                                                        turn_lens=tl))
+
+
+def sdpa_bytes(case: SdpaCase) -> int:
+    """Algorithmic bytes of one dvattn_sdpa call: attended K+V rows of each worker + the
+    per-turn queries + out + locations (padding past a worker's location is not counted)."""
+    F, W, Hq, S, E = case.rotated.shape
+    es = ESIZE[case.dtype]
+    loc = case.locations.cpu().numpy().astype(np.int64)
+    L = case.fragment_lengths.cpu().numpy().astype(np.int64)
+    rows = np.array([k.size(-2) for k in case.keys], dtype=np.int64)
+    Hkv = case.keys[0].size(-3)
+    n = np.clip(np.minimum(loc.max(axis=2) + 1, np.minimum(L, rows)[:, None]), 0, None).sum()
+    return int(n) * Hkv * 2 * E * es + case.rotated.numel() * es + W * Hq * S * E * es + case.locations.numel() * 4
+
+
 def config3(device="cpu", seed: int = 3, L: int = 131072, W: int = 4) -> PagedCase:
     """fp16 long context: W=4, 128/8 heads, E=128, R=128 (full rotary), L=131072, page 64, one turn."""
     return make_paged([[L]] * W, Hq=128, Hkv=8, E=128, R=128, BS=64, dtype=torch.float16, seed=seed, device=device)

@@ -119,6 +119,31 @@ typedef struct dvattn_sdpa_args {
     float* out_f32;                     /* optional [W,Hq,S,Ev] f32 copy of the output     */
 } dvattn_sdpa_args;
 
+/*
+ * Arguments of one paged KV append with fused K rotation (the step before the attention
+ * path): the new tokens of worker w, keys rotated like apply_rotary_pos_emb, are written
+ * at logical positions positions[w], positions[w]+1, ... of its block table.
+ */
+typedef struct dvattn_append_args {
+    int dtype;
+    int W, Hkv, E, Ev;
+    int n;                        /* new tokens per worker in keys/values (with padding) */
+    int R;                        /* rotary dim = cosines.size(2); 0: keys not rotated   */
+    int block_size;
+    int max_blocks_per_seq;
+    long long num_blocks;
+    void* k_cache;                /* [NB,BS,Hkv,E] T, written                            */
+    void* v_cache;                /* [NB,BS,Hkv,Ev] T, written                           */
+    const void* keys;             /* [W,Hkv,n,E] T, unrotated                            */
+    const void* values;           /* [W,Hkv,n,Ev] T                                      */
+    const float* cosines;         /* [W,n,R] f32, full width (both halves read)          */
+    const float* sines;           /* [W,n,R] f32                                         */
+    const int* block_tables;      /* [W,max_blocks] i32                                  */
+    const int* positions;         /* [W] i32: logical position of worker w's first new token */
+    const int* counts;            /* [W] i32 or null: only the last counts[w] of the n tokens
+                                     are new (left padding); null = all n               */
+} dvattn_append_args;
+
 /* ABI version of this header (bumped on any layout change of the structs above). */
 int dvattn_abi_version(void);
 
@@ -207,6 +232,15 @@ size_t dvattn_sdpa_workspace_size(const dvattn_sdpa_args* args);
  * (src/binding.cu:356-372) is dvattn_rope into the rotated-query buffer followed by this.
  */
 int dvattn_sdpa(const dvattn_sdpa_args* args, void* workspace, size_t workspace_bytes, dvattn_stream_t stream);
+
+/*
+ * Paged KV append with fused K rotation.  Replaces the reference's PyTorch cache update
+ * (apply_rotary_pos_emb on the new keys + DynamicCache append, python/dvattn/attention.py:
+ * 131-149, 302-304; the re-rotation of merge_caches, :245-251, is the same call with the
+ * cos/sin of the target offset).  Positions outside the block table and pages outside
+ * [0, num_blocks) are skipped.
+ */
+int dvattn_paged_append(const dvattn_append_args* args, dvattn_stream_t stream);
 
 /*
  * Standalone query rotation, schema `dvattn_rope` (src/binding.cu:41-77, src/rope.cuh:2-65):

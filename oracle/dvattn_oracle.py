@@ -303,3 +303,37 @@ def paged_via_sdpa_pt(scale, locations, queries, cosines, sines, fragment_length
                                            half_to_full(sines[f].cpu(), R), unsqueeze_dim=1) for f in range(F)])
     out, lse = sdpa_pt(rq, loc, keys, values, scale, return_lse=True)
     return out, lse
+
+
+# ---------------------------------------------------------------------------------
+# paged KV append with K rotation: apply_rotary_pos_emb on the new keys
+# (python/dvattn/attention.py:302-304) + the cache update of the last counts[w] tokens
+# (attention.py:131-149), written through the block table
+# ---------------------------------------------------------------------------------
+def paged_append(k_cache, v_cache, keys, values, cosines, sines, block_tables, positions, counts=None):
+    """Returns updated copies of k_cache / v_cache (CPU)."""
+    k_cache, v_cache = k_cache.clone().cpu(), v_cache.clone().cpu()
+    keys, values = keys.cpu(), values.cpu()
+    W, Hkv, n, E = keys.shape
+    R = cosines.size(2)
+    if R:
+        rk = apply_rotary_pos_emb(keys, cosines.cpu(), sines.cpu(), unsqueeze_dim=1)
+    else:
+        rk = keys
+    bt = block_tables.cpu().numpy()
+    pos = positions.cpu().numpy()
+    cnt = counts.cpu().numpy() if counts is not None else np.full(W, n)
+    NB, BS = k_cache.shape[:2]
+    for w in range(W):
+        c = int(max(0, min(n, cnt[w])))
+        for i in range(c):
+            t = n - c + i
+            lp = int(pos[w]) + i
+            if lp < 0 or lp >= bt.shape[1] * BS:
+                continue
+            page = int(bt[w, lp // BS])
+            if page < 0 or page >= NB:
+                continue
+            k_cache[page, lp % BS] = rk[w, :, t]
+            v_cache[page, lp % BS] = values[w, :, t]
+    return k_cache, v_cache

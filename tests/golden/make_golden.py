@@ -184,7 +184,22 @@ def main():
                                                           seed=34, skip_turns=(0,)))
 
 
+def golden_append(ref, name, W, Hkv, n, E, R, dtype, seed):
+    """K rotation of new tokens with the reference's apply_rotary_pos_emb (the keys the
+    paged append writes)."""
+    g = torch.Generator().manual_seed(seed)
+    keys = torch.randn((W, Hkv, n, E), generator=g).to(dtype)
+    pos = torch.randint(0, 8192, (W, n), generator=g)
+    cos, sin = wl.rope_angles(pos, R)
+    rk = ref.apply_rotary_pos_emb(keys, cos, sin) if R else keys.clone()
+    fixtures.save(name, dict(keys=keys, cosines=cos, sines=sin, rotated=rk), dict(kind="append"))
+    print("wrote", name, tuple(rk.shape))
+
+
 def sdpa_only(ref):
+    golden_append(ref, "append_bf16_r64", 3, 2, 17, 128, 64, torch.bfloat16, 51)
+    golden_append(ref, "append_f16_r128", 2, 4, 9, 128, 128, torch.float16, 52)
+    golden_append(ref, "append_f32_e64_r32", 2, 1, 5, 64, 32, torch.float32, 53)
     bf, hf, f32 = torch.bfloat16, torch.float16, torch.float32
     golden_sdpa(ref, "sdpa_bf16_w4", wl.make_sdpa([37, 90], W=4, Hq=32, Hkv=2, E=128, R=64, dtype=bf, seed=31))
     golden_sdpa(ref, "sdpa_f16_e256_shared_s2", wl.make_sdpa([20, 5, 61], W=3, Hq=16, Hkv=1, E=256, R=64, dtype=hf,
