@@ -748,7 +748,7 @@ def run_append(args, world, rank, local):
             "dtype": "bfloat16", "data": "synthetic (seeded)",
             "config": {"workload": "append4: 16 workers x U[1,2048] new tokens (padded to 2048), 2/128 KV heads, "
                                    "R=32, page 16", "bytes_per_step_per_gpu": nbytes,
-                       "parallelism": f"batch-replica x{world}", "l2": "3 rotating new-token sets (34 MB each); the cache (2.3 GB) is written once per step"},
+                       "parallelism": f"batch-replica x{world}", "l2": "3 rotating new-token sets (34 MB each); each step writes its rows of a 302 MB cache"},
             "roofline": {"bound": "hbm", "kernel": "paged_append_kernel",
                          "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak,
                          "peak_kind": peak_kind, "unit": "GB/s",

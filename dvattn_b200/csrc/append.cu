@@ -13,8 +13,8 @@
 // and o[e+R/2] = x[e+R/2]*c[e+R/2] + x[e]*s[e+R/2] (full-width cos/sin rows, both
 // halves read), dims e >= R copied; f32 math, one rounding to T.
 //
-// One thread per 16-byte chunk of a (token, head) row of K or V: a K chunk in the first
-// rotary half also reads its partner chunk R/2 further, and vice versa.  HBM-bound.
+// A warp per new token, a lane per 16-byte chunk of its K / V rows: a K chunk in the
+// first rotary half also reads its partner chunk R/2 further, and vice versa.  HBM-bound.
 #include "decode.cuh"
 
 namespace dvb {
@@ -44,15 +44,17 @@ __device__ __forceinline__ float rot_k(const T* x, const float* c, const float* 
     return v;
 }
 
+// One warp per (worker, token): the page lookup is done once per token and the lanes
+// cover the token's 16-byte chunks of K (all heads) and V (all heads).
 template <class T>
 __global__ void __launch_bounds__(256) paged_append_kernel(AppendParams p) {
     constexpr int PER = 16 / sizeof(T);  // elements per 16-byte chunk
     const int ck = p.E / PER, cv = p.Ev / PER;
-    const long long per_tok = (long long)p.Hkv * (ck + cv);
-    const long long tot = (long long)p.W * p.n * per_tok;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tot; i += (long long)gridDim.x * blockDim.x) {
-        const long long wt = i / per_tok;
-        int j = (int)(i - wt * per_tok);
+    const int per_tok = p.Hkv * (ck + cv);
+    const int lane = threadIdx.x & 31;
+    const long long ntok = (long long)p.W * p.n;
+    const long long nwarp = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long wt = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5); wt < ntok; wt += nwarp) {
         const int w = (int)(wt / p.n), t = (int)(wt - (long long)w * p.n);
         const int cnt = p.cnt ? __ldg(p.cnt + w) : p.n;
         const int first = p.n - (cnt < p.n ? (cnt > 0 ? cnt : 0) : p.n);
@@ -62,32 +64,34 @@ __global__ void __launch_bounds__(256) paged_append_kernel(AppendParams p) {
         const int page = __ldg(p.bt + (size_t)w * p.maxb + lp / p.BS);
         if (page < 0 || page >= p.NB) continue;
         const long long slot = (long long)page * p.BS + lp % p.BS;
-        const bool is_k = j < p.Hkv * ck;
-        if (!is_k) j -= p.Hkv * ck;
-        const int cpr = is_k ? ck : cv, Ed = is_k ? p.E : p.Ev;
-        const int h = j / cpr, c = j - h * cpr;
-        const size_t src_row = (((size_t)w * p.Hkv + h) * p.n + t) * Ed;
-        const size_t dst_row = ((size_t)slot * p.Hkv + h) * Ed;
-        if (!is_k) {
-            const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.values) + src_row + c * PER);
-            *reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + dst_row + c * PER) = v;
-            continue;
-        }
-        const T* x = static_cast<const T*>(p.keys) + src_row;
-        T* dst = static_cast<T*>(p.k_cache) + dst_row + c * PER;
-        const int e0 = c * PER;
-        if (e0 >= p.R) {  // pass-through chunk
-            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(x + e0);
-            continue;
-        }
         const size_t crow = ((size_t)w * p.n + t) * p.R;
-        const float* cr = p.cos + crow;
-        const float* sr = p.sin + crow;
-        alignas(16) T o[PER];
+        for (int j = lane; j < per_tok; j += 32) {
+            const bool is_k = j < p.Hkv * ck;
+            const int jj = is_k ? j : j - p.Hkv * ck;
+            const int cpr = is_k ? ck : cv, Ed = is_k ? p.E : p.Ev;
+            const int h = jj / cpr, c = jj - h * cpr;
+            const size_t src_row = (((size_t)w * p.Hkv + h) * p.n + t) * Ed;
+            const size_t dst_row = ((size_t)slot * p.Hkv + h) * Ed;
+            if (!is_k) {
+                const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.values) + src_row + c * PER);
+                *reinterpret_cast<uint4*>(static_cast<T*>(p.v_cache) + dst_row + c * PER) = v;
+                continue;
+            }
+            const T* x = static_cast<const T*>(p.keys) + src_row;
+            T* dst = static_cast<T*>(p.k_cache) + dst_row + c * PER;
+            const int e0 = c * PER;
+            if (e0 >= p.R) {  // pass-through chunk
+                *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(x + e0);
+                continue;
+            }
+            const float* cr = p.cos + crow;
+            const float* sr = p.sin + crow;
+            alignas(16) T o[PER];
 #pragma unroll
-        for (int u = 0; u < PER; ++u) o[u] = Elem<T>::from_f(e0 + u < p.R ? rot_k(x, cr, sr, e0 + u, p.R)
-                                                                        : Elem<T>::to_f(x[e0 + u]));
-        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
+            for (int u = 0; u < PER; ++u)
+                o[u] = Elem<T>::from_f(e0 + u < p.R ? rot_k(x, cr, sr, e0 + u, p.R) : Elem<T>::to_f(x[e0 + u]));
+            *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(o);
+        }
     }
 }
 
@@ -110,11 +114,10 @@ int paged_append_launch(const dvattn_append_args* a, cudaStream_t stream) {
     p.BS = a->block_size; p.maxb = a->max_blocks_per_seq; p.NB = a->num_blocks;
     p.k_cache = a->k_cache; p.v_cache = a->v_cache; p.keys = a->keys; p.values = a->values;
     p.cos = a->cosines; p.sin = a->sines; p.bt = a->block_tables; p.pos = a->positions; p.cnt = a->counts;
-    const long long chunks = (long long)a->W * a->n * a->Hkv * ((a->E + a->Ev) * esz / 16);
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long want = (chunks + 255) / 256;
+    const long long want = ((long long)a->W * a->n + 7) / 8;  // 8 warps (tokens) per block
     const int grid = (int)(want < (long long)sms * 8 ? want : (long long)sms * 8);
     switch (a->dtype) {
         case DVATTN_FLOAT16: paged_append_kernel<__half><<<grid, 256, 0, stream>>>(p); break;

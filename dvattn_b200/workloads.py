@@ -394,7 +394,7 @@ def config2_sdpa(device="cpu", seed: int = 2, W: int = 32) -> SdpaCase:
     rq = _randn((F, W, Hq, 1, E), torch.bfloat16, gen, device)
     keys = [_randn((W, Hkv, int(Lf[f]), E), torch.bfloat16, gen, device) for f in range(F)]
     vals = [_randn((W, Hkv, int(Lf[f]), E), torch.bfloat16, gen, device) for f in range(F)]
-    loc = torch.from_numpy((tl.T - 1).astype(np.int32)).reshape(F, W, 1).to(device)
+    loc = torch.from_numpy(np.ascontiguousarray(tl.T - 1, dtype=np.int32)).reshape(F, W, 1).contiguous().to(device)
     z = torch.zeros((F, W, 1, 0), dtype=torch.float32, device=device)
     return SdpaCase(queries=q, rotated=rq, cosines=z, sines=z.clone(), locations=loc,
                     fragment_lengths=torch.from_numpy(Lf.astype(np.int32)).to(device), keys=keys, values=vals,
