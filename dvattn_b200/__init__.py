@@ -30,6 +30,7 @@ _load()
 
 from .api import (  # noqa: E402
     apply_rotary_pos_emb,
+    dvattn_build_views,
     dvattn_fused,
     dvattn_lse_merge,
     dvattn_paged_append,
@@ -43,6 +44,7 @@ from .api import (  # noqa: E402
 
 __all__ = [
     "apply_rotary_pos_emb",
+    "dvattn_build_views",
     "dvattn_fused",
     "dvattn_lse_merge",
     "dvattn_paged_append",

@@ -80,6 +80,30 @@ def dvattn_varlen_paged_sdpa(queries: torch.Tensor, locations: torch.Tensor, cos
     return out
 
 
+_ROUND = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
+
+
+def dvattn_build_views(seg_lengths: torch.Tensor, seg_order: torch.Tensor, n: int, R: int, rope_base: float,
+                       attention_scaling: float = 1.0, dtype=torch.float32):
+    """Turn/view metadata on the GPU (DVAttnCache.update, attention.py:161-191): for F
+    segments with lengths seg_lengths [F] i32 and each worker's segment order seg_order
+    [W, F] i32 (index of segment f in worker w's list), the locations [F, W, n] of the n new
+    tokens and their cos/sin [F, W, n, R] f32 from the model's rotary embedding (base
+    ``rope_base``, scaled, rounded through ``dtype`` as the model returns them)."""
+    F, W = seg_lengths.size(0), seg_order.size(0)
+    dev = seg_lengths.device
+    loc = torch.empty((F, W, n), dtype=torch.int32, device=dev)
+    cos = torch.empty((F, W, n, R), dtype=torch.float32, device=dev)
+    sin = torch.empty((F, W, n, R), dtype=torch.float32, device=dev)
+    # the inverse frequencies exactly as the model's rotary module computes them (on the host)
+    inv_freq = None
+    if R:
+        inv_freq = (1.0 / (rope_base ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))).to(dev)
+    _ops.dvattn_build_views(loc, cos, sin, seg_lengths, seg_order, inv_freq, rope_base, attention_scaling,
+                            _ROUND[dtype])
+    return loc, cos, sin
+
+
 def dvattn_paged_append(k_cache: torch.Tensor, v_cache: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
                         cosines: torch.Tensor, sines: torch.Tensor, block_tables: torch.Tensor,
                         positions: torch.Tensor, counts: Optional[torch.Tensor] = None) -> None:

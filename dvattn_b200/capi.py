@@ -51,6 +51,7 @@ EXPORTS = [
     "dvattn_sdpa_workspace_size",
     "dvattn_sdpa",
     "dvattn_paged_append",
+    "dvattn_build_views",
 ]
 
 _vp = ctypes.c_void_p

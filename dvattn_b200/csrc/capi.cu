@@ -35,6 +35,10 @@ int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace, si
     return dvb::varlen_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), DVATTN_PHASE_ALL);
 }
 
+int dvattn_build_views(const dvattn_views_args* args, dvattn_stream_t stream) {
+    return dvb::build_views_launch(args, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int dvattn_paged_append(const dvattn_append_args* args, dvattn_stream_t stream) {
     return dvb::paged_append_launch(args, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -12,6 +12,8 @@ int decode_launch(const dvattn_paged_args* a, void* workspace, size_t wbytes, cu
 
 size_t varlen_workspace_size(const dvattn_varlen_args* a);
 int varlen_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
+// turn/view metadata (views.cu)
+int build_views_launch(const dvattn_views_args* a, cudaStream_t stream);
 // paged KV append with fused K rotation (append.cu)
 int paged_append_launch(const dvattn_append_args* a, cudaStream_t stream);
 // contiguous fragments (the dvattn_sdpa op)

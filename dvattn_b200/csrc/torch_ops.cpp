@@ -315,6 +315,46 @@ void dvattn_lse_merge_op(at::Tensor& out, const c10::optional<at::Tensor>& lse_o
 }
 
 // ---------------------------------------------------------------------------------
+// dvattn_build_views (B200 addition): locations and cos/sin of the turn/view structure
+// ---------------------------------------------------------------------------------
+void dvattn_build_views_op(at::Tensor& locations, at::Tensor& cosines, at::Tensor& sines, const at::Tensor& seg_lengths,
+                           const at::Tensor& seg_order, const c10::optional<at::Tensor>& inv_freq, double rope_base,
+                           double attention_scaling, int64_t round_dtype) {
+    const c10::cuda::CUDAGuard guard(locations.device());
+    TORCH_CHECK(locations.dim() == 3 && cosines.dim() == 4 && sines.dim() == 4 && seg_lengths.dim() == 1 &&
+                    seg_order.dim() == 2, "dvattn_build_views: wrong tensor ranks");
+    check_i32(locations, "locations");
+    check_i32(seg_lengths, "seg_lengths");
+    check_i32(seg_order, "seg_order");
+    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat,
+                "dvattn_build_views: cosines/sines must be float32");
+    check_all(locations, {Named{&locations, "locations"}, Named{&cosines, "cosines"}, Named{&sines, "sines"},
+                          Named{&seg_lengths, "seg_lengths"}, Named{&seg_order, "seg_order"}});
+    const int F = locations.size(0), W = locations.size(1), n = locations.size(2), R = cosines.size(3);
+    TORCH_CHECK(seg_lengths.size(0) == F && seg_order.size(0) == W && seg_order.size(1) == F,
+                "dvattn_build_views: seg_lengths [F], seg_order [W, F]");
+    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == W && cosines.size(2) == n && sines.sizes() == cosines.sizes(),
+                "dvattn_build_views: cosines/sines must be [F, W, n, R]");
+    dvattn_views_args a{};
+    a.F = F; a.W = W; a.n = n; a.R = R;
+    a.rope_base = static_cast<float>(rope_base);
+    a.attention_scaling = static_cast<float>(attention_scaling);
+    a.round_dtype = static_cast<int>(round_dtype);
+    a.seg_lengths = seg_lengths.const_data_ptr<int>();
+    a.seg_order = seg_order.const_data_ptr<int>();
+    if (inv_freq.has_value()) {
+        check_cuda_tensor(*inv_freq, "inv_freq", locations);
+        TORCH_CHECK(inv_freq->scalar_type() == at::kFloat && inv_freq->numel() == R / 2,
+                    "dvattn_build_views: inv_freq must be f32 [R/2]");
+        a.inv_freq = inv_freq->const_data_ptr<float>();
+    }
+    a.locations = locations.data_ptr<int>();
+    a.cosines = cosines.data_ptr<float>();
+    a.sines = sines.data_ptr<float>();
+    check_status(dvattn_build_views(&a, cur_stream(locations)), "dvattn_build_views");
+}
+
+// ---------------------------------------------------------------------------------
 // dvattn_paged_append (B200 addition): the new tokens' keys rotated as
 // apply_rotary_pos_emb and written with their values into the workers' pages
 // ---------------------------------------------------------------------------------
@@ -480,6 +520,8 @@ TORCH_LIBRARY(libdvatt, m) {
           "Tensor locations, Tensor queries, Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, "
           "Tensor v_cache, Tensor block_tables, Tensor cu_seqlens_q, Tensor cu_seqlens_k) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
     m.def("dvattn_lse_merge(Tensor(a!) output, Tensor(b!)? lse_out, Tensor part_out, Tensor part_lse) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_build_views(Tensor(a!) locations, Tensor(b!) cosines, Tensor(c!) sines, Tensor seg_lengths, "
+          "Tensor seg_order, Tensor? inv_freq, float rope_base, float attention_scaling, int round_dtype) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
     m.def("dvattn_paged_append(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor keys, Tensor values, Tensor cosines, "
           "Tensor sines, Tensor block_tables, Tensor positions, Tensor? counts) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
 }
@@ -495,4 +537,5 @@ TORCH_LIBRARY_IMPL(libdvatt, CUDA, m) {
     m.impl("dvattn_varlen_paged_sdpa_ex", dvattn_varlen_paged_sdpa_ex_op);
     m.impl("dvattn_lse_merge", dvattn_lse_merge_op);
     m.impl("dvattn_paged_append", dvattn_paged_append_op);
+    m.impl("dvattn_build_views", dvattn_build_views_op);
 }

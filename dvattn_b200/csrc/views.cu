@@ -1,0 +1,70 @@
+// Device-side turn/view metadata (the bookkeeping before the attention path).
+//
+// Reference behaviour replaced: DVAttnCache.update at layer 0 (python/dvattn/attention.py:
+// 161-191) walks every worker's list of cache segments on the host: for worker w and the
+// segment at list index k, the new tokens' location in that segment is
+//     loc = (sum of the lengths of the segments at index >= k in w's list) - n + i,
+// i = 0..n-1 (arange(pos - n, pos) after pos += length, iterating the list backwards);
+// then the model's rotary embedding turns the locations into cos/sin
+// (attention.py:185: cos(loc * inv_freq), inv_freq_j = base^(-2j/R), both halves equal,
+// times attention_scaling, returned in the model dtype and widened to f32), followed by a
+// torch._dynamo.graph_break.  Here one kernel writes locations [F, W, n] and cos/sin
+// [F, W, n, R] from the segment lengths and each worker's segment order.
+#include "decode.cuh"
+
+namespace dvb {
+
+template <class R> __device__ __forceinline__ float round_through(float x) { return Elem<R>::to_f(Elem<R>::from_f(x)); }
+
+__global__ void __launch_bounds__(256) build_views_kernel(dvattn_views_args a) {
+    const long long tot = (long long)a.F * a.W * a.n;
+    const int hr = a.R >> 1;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < tot;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const int i = (int)(idx % a.n);
+        const long long fw = idx / a.n;
+        const int w = (int)(fw % a.W), f = (int)(fw / a.W);
+        const int k = __ldg(a.seg_order + (size_t)w * a.F + f);
+        long long suffix = 0;  // lengths of the segments from index k to the end of w's list
+        for (int g = 0; g < a.F; ++g)
+            if (__ldg(a.seg_order + (size_t)w * a.F + g) >= k) suffix += __ldg(a.seg_lengths + g);
+        const int loc = (int)(suffix - a.n + i);
+        a.locations[idx] = loc;
+        if (hr == 0) continue;
+        float* cr = a.cosines + idx * a.R;
+        float* sr = a.sines + idx * a.R;
+        const float pos = (float)loc;
+        for (int j = 0; j < hr; ++j) {
+            // inv_freq_j = 1 / base^(2j / R) in f32, freq = inv_freq_j * pos (one rounding)
+            const float inv = a.inv_freq ? __ldg(a.inv_freq + j) : 1.0f / powf(a.rope_base, (float)(2 * j) / (float)a.R);
+            const float ang = __fmul_rn(inv, pos);
+            float c = cosf(ang) * a.attention_scaling, s = sinf(ang) * a.attention_scaling;
+            if (a.round_dtype == DVATTN_BFLOAT16) {
+                c = round_through<__nv_bfloat16>(c);
+                s = round_through<__nv_bfloat16>(s);
+            } else if (a.round_dtype == DVATTN_FLOAT16) {
+                c = round_through<__half>(c);
+                s = round_through<__half>(s);
+            }
+            cr[j] = cr[j + hr] = c;
+            sr[j] = sr[j + hr] = s;
+        }
+    }
+}
+
+int build_views_launch(const dvattn_views_args* a, cudaStream_t stream) {
+    if (!a) return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->F < 0 || a->W < 0 || a->n < 0 || a->R < 0 || (a->R & 1) || a->round_dtype < 0 || a->round_dtype > 2)
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    const long long tot = (long long)a->F * a->W * a->n;
+    if (tot == 0) return DVATTN_OK;
+    if (!a->seg_lengths || !a->seg_order || !a->locations || (a->R > 0 && (!a->cosines || !a->sines)))
+        return DVATTN_ERR_INVALID_ARGUMENT;
+    if (a->R > 0 && !(a->rope_base > 0.f)) return DVATTN_ERR_INVALID_ARGUMENT;
+    const long long want = (tot + 255) / 256;
+    const int grid = (int)(want < 148LL * 16 ? want : 148LL * 16);
+    build_views_kernel<<<grid, 256, 0, stream>>>(*a);
+    return cudaGetLastError() == cudaSuccess ? DVATTN_OK : DVATTN_ERR_CUDA;
+}
+
+}  // namespace dvb

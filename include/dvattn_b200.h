@@ -144,6 +144,25 @@ typedef struct dvattn_append_args {
                                      are new (left padding); null = all n               */
 } dvattn_append_args;
 
+/*
+ * Arguments of the turn/view metadata builder: for F cache segments shared by W workers
+ * (each worker lists the segments in its own order) and n new tokens per worker.
+ */
+typedef struct dvattn_views_args {
+    int F, W, n;
+    int R;                        /* rotary dim of the cos/sin rows; 0: locations only    */
+    float rope_base;              /* theta of the model's rotary embedding                */
+    float attention_scaling;      /* factor on cos/sin (1 for the default rotary)         */
+    int round_dtype;              /* DVATTN_*: cos/sin rounded through the model dtype    */
+    const int* seg_lengths;       /* [F] i32: length of each segment                      */
+    const int* seg_order;         /* [W,F] i32: index of segment f in worker w's list     */
+    const float* inv_freq;        /* [R/2] f32 or null: the model's inverse frequencies
+                                     (null: 1 / rope_base^(2j/R) computed on the device) */
+    int* locations;               /* out [F,W,n] i32                                      */
+    float* cosines;               /* out [F,W,n,R] f32 (both halves equal)                */
+    float* sines;                 /* out [F,W,n,R] f32                                    */
+} dvattn_views_args;
+
 /* ABI version of this header (bumped on any layout change of the structs above). */
 int dvattn_abi_version(void);
 
@@ -241,6 +260,13 @@ int dvattn_sdpa(const dvattn_sdpa_args* args, void* workspace, size_t workspace_
  * [0, num_blocks) are skipped.
  */
 int dvattn_paged_append(const dvattn_append_args* args, dvattn_stream_t stream);
+
+/*
+ * Turn/view metadata on the GPU: replaces the host loops of DVAttnCache.update
+ * (python/dvattn/attention.py:161-191: per-(segment, worker) locations, then the model's
+ * rotary embedding of them).  Writes the locations, cosines and sines the attention ops take.
+ */
+int dvattn_build_views(const dvattn_views_args* args, dvattn_stream_t stream);
 
 /*
  * Standalone query rotation, schema `dvattn_rope` (src/binding.cu:41-77, src/rope.cuh:2-65):

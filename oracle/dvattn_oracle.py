@@ -337,3 +337,32 @@ def paged_append(k_cache, v_cache, keys, values, cosines, sines, block_tables, p
             k_cache[page, lp % BS] = rk[w, :, t]
             v_cache[page, lp % BS] = values[w, :, t]
     return k_cache, v_cache
+
+
+# ---------------------------------------------------------------------------------
+# turn/view metadata: DVAttnCache.update at layer 0 (python/dvattn/attention.py:161-191)
+# and the model's default rotary embedding of the locations (HF rotary: inv_freq =
+# 1 / base^(arange(0, R, 2) / R) in f32, freqs = inv_freq * pos, emb = cat(freqs, freqs),
+# cos/sin times attention_scaling, returned in the model dtype, widened to f32)
+# ---------------------------------------------------------------------------------
+def build_views(seg_lengths, seg_order, n, R, rope_base, attention_scaling=1.0, dtype=torch.float32):
+    lens = [int(x) for x in seg_lengths]
+    order = np.asarray(seg_order)
+    F, W = len(lens), order.shape[0]
+    loc = torch.zeros((F, W, n), dtype=torch.int32)
+    for w in range(W):
+        # worker w's list, then the backward walk of the reference
+        lst = sorted(range(F), key=lambda f: order[w, f])
+        pos = 0
+        for f in reversed(lst):
+            pos += lens[f]
+            loc[f, w] = torch.arange(pos - n, pos, dtype=torch.int32)
+    if R == 0:
+        z = torch.zeros((F, W, n, 0))
+        return loc, z, z.clone()
+    inv_freq = 1.0 / (rope_base ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))
+    freqs = loc.float()[..., None] * inv_freq
+    emb = torch.cat((freqs, freqs), dim=-1)
+    cos = (emb.cos() * attention_scaling).to(dtype).to(torch.float32)
+    sin = (emb.sin() * attention_scaling).to(dtype).to(torch.float32)
+    return loc, cos, sin

@@ -196,7 +196,32 @@ def golden_append(ref, name, W, Hkv, n, E, R, dtype, seed):
     print("wrote", name, tuple(rk.shape))
 
 
+def golden_views(name, lens, order, n, R, theta, dtype):
+    """cos/sin of the turn/view locations from HF's LlamaRotaryEmbedding, the module the
+    reference calls as model.rotary_emb (python/dvattn/attention.py:185), on the locations
+    of DVAttnCache.update's walk (restated in oracle.build_views)."""
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+    sys.path.insert(0, ROOT)
+    from oracle import dvattn_oracle as O
+    lens = np.asarray(lens, np.int32)
+    order = np.asarray(order, np.int32)
+    loc, _, _ = O.build_views(lens, order, n, R, theta, 1.0, dtype)
+    cfg = LlamaConfig(hidden_size=R * 8, num_attention_heads=8, num_key_value_heads=2, rope_theta=theta,
+                      max_position_embeddings=1 << 20)
+    emb = LlamaRotaryEmbedding(cfg)
+    F, W = loc.shape[:2]
+    c, s_ = emb(torch.zeros(1, 1, R, dtype=dtype), loc.reshape(F * W, n).long())
+    fixtures.save(name, dict(seg_lengths=torch.from_numpy(lens), seg_order=torch.from_numpy(order), locations=loc,
+                             cosines=c.float().reshape(F, W, n, R), sines=s_.float().reshape(F, W, n, R)),
+                  dict(kind="views", n=n, R=R, theta=theta, dtype=str(dtype).replace("torch.", "")))
+    print("wrote", name)
+
+
 def sdpa_only(ref):
+    golden_views("views_bf16_theta1e6", [1200, 35, 77000], [[0, 1, 2], [2, 0, 1], [1, 2, 0], [0, 2, 1]], 5, 128,
+                 1000000.0, torch.bfloat16)
+    golden_views("views_f32_theta1e4", [64, 9], [[1, 0], [0, 1]], 3, 64, 10000.0, torch.float32)
     golden_append(ref, "append_bf16_r64", 3, 2, 17, 128, 64, torch.bfloat16, 51)
     golden_append(ref, "append_f16_r128", 2, 4, 9, 128, 128, torch.float16, 52)
     golden_append(ref, "append_f32_e64_r32", 2, 1, 5, 64, 32, torch.float32, 53)
