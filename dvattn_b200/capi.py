@@ -83,6 +83,19 @@ class SdpaArgs(ctypes.Structure):
                 ("fragment_batch", ctypes.POINTER(_i)), ("lse_out", _vp), ("out_f32", _vp)]
 
 
+class AppendArgs(ctypes.Structure):
+    _fields_ = [("dtype", _i), ("W", _i), ("Hkv", _i), ("E", _i), ("Ev", _i), ("n", _i), ("R", _i),
+                ("block_size", _i), ("max_blocks_per_seq", _i), ("num_blocks", ctypes.c_longlong),
+                ("k_cache", _vp), ("v_cache", _vp), ("keys", _vp), ("values", _vp), ("cosines", _vp),
+                ("sines", _vp), ("block_tables", _vp), ("positions", _vp), ("counts", _vp)]
+
+
+class ViewsArgs(ctypes.Structure):
+    _fields_ = [("F", _i), ("W", _i), ("n", _i), ("R", _i), ("rope_base", ctypes.c_float),
+                ("attention_scaling", ctypes.c_float), ("round_dtype", _i), ("seg_lengths", _vp),
+                ("seg_order", _vp), ("inv_freq", _vp), ("locations", _vp), ("cosines", _vp), ("sines", _vp)]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -122,6 +135,10 @@ def lib() -> ctypes.CDLL:
         L.dvattn_varlen_rope.argtypes = [_i] * 6 + [_vp] * 5
         L.dvattn_lse_merge.restype = _i
         L.dvattn_lse_merge.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp, _vp]
+        L.dvattn_paged_append.restype = _i
+        L.dvattn_paged_append.argtypes = [ctypes.POINTER(AppendArgs), _vp]
+        L.dvattn_build_views.restype = _i
+        L.dvattn_build_views.argtypes = [ctypes.POINTER(ViewsArgs), _vp]
         _lib = L
     return _lib
 
@@ -280,25 +297,67 @@ def lse_merge(part_out, part_lse, out, lse_out=None):
     return out
 
 
+class SdpaCall:
+    """A prepared dvattn_sdpa call through the C ABI: queries [F,W,Hq,S,E] (rotated),
+    keys/values lists of F tensors [Hkv,L,E] or [B,Hkv,L,E] (B = 1 or W); argument struct,
+    fragment pointer arrays and workspace kept across launches."""
+
+    def __init__(self, out, scale, locations, queries, fragment_lengths, keys, values, lse=None, out_f32=None,
+                 workspace: Optional[torch.Tensor] = None):
+        W, Hq, S, Ev = out.shape
+        F, E = locations.size(0), queries.size(4)
+        batched = keys[0].dim() == 4
+        fo = 1 if batched else 0
+        self._kp = (_vp * F)(*[k.data_ptr() for k in keys])
+        self._vp = (_vp * F)(*[v.data_ptr() for v in values])
+        self._rows = (_i * F)(*[k.size(fo + 1) for k in keys])
+        self._batch = (_i * F)(*[(k.size(0) if batched else 1) for k in keys])
+        self._keep = (out, locations, queries, fragment_lengths, keys, values, lse, out_f32)
+        self.args = SdpaArgs(_DTYPE.get(out.dtype, -1), F, W, Hq, keys[0].size(fo), E, Ev, S, float(scale),
+                             out.data_ptr(), queries.data_ptr(), locations.data_ptr(), fragment_lengths.data_ptr(),
+                             self._kp, self._vp, self._rows, self._batch, _ptr(lse), _ptr(out_f32))
+        n = lib().dvattn_sdpa_workspace_size(ctypes.byref(self.args))
+        if n == 0 and W * S > 0 and Hq > 0:
+            raise DvattnError(lib().dvattn_sdpa(ctypes.byref(self.args), None, 0, None), "dvattn_sdpa workspace size")
+        if workspace is None:
+            workspace = torch.empty(max(n, 256), dtype=torch.uint8, device=out.device)
+        self.workspace = workspace
+
+    def __call__(self, stream: Optional[torch.cuda.Stream] = None) -> None:
+        st = lib().dvattn_sdpa(ctypes.byref(self.args), self.workspace.data_ptr(), self.workspace.numel(),
+                               _stream(stream))
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_sdpa")
+
+
 def sdpa(out, scale, locations, queries, fragment_lengths, keys, values, lse=None, out_f32=None):
-    """dvattn_sdpa through the C ABI: queries [F,W,Hq,S,E] (rotated), keys/values lists of F
-    tensors [Hkv,L,E] or [B,Hkv,L,E] (B = 1 or W)."""
-    W, Hq, S, Ev = out.shape
-    F, E = locations.size(0), queries.size(4)
-    batched = keys[0].dim() == 4
-    fo = 1 if batched else 0
-    kp = (_vp * F)(*[k.data_ptr() for k in keys])
-    vp = (_vp * F)(*[v.data_ptr() for v in values])
-    rows = (_i * F)(*[k.size(fo + 1) for k in keys])
-    batch = (_i * F)(*[(k.size(0) if batched else 1) for k in keys])
-    a = SdpaArgs(_DTYPE.get(out.dtype, -1), F, W, Hq, keys[0].size(fo), E, Ev, S, float(scale), out.data_ptr(),
-                 queries.data_ptr(), locations.data_ptr(), fragment_lengths.data_ptr(), kp, vp, rows, batch,
-                 lse.data_ptr() if lse is not None else None, out_f32.data_ptr() if out_f32 is not None else None)
-    n = lib().dvattn_sdpa_workspace_size(ctypes.byref(a))
-    if n == 0 and W * S > 0 and Hq > 0:
-        raise DvattnError(lib().dvattn_sdpa(ctypes.byref(a), None, 0, None), "dvattn_sdpa workspace size")
-    ws = torch.empty(max(n, 256), dtype=torch.uint8, device=out.device)
-    st = lib().dvattn_sdpa(ctypes.byref(a), ws.data_ptr(), ws.numel(), _stream(None))
-    if st != DVATTN_OK:
-        raise DvattnError(st, "dvattn_sdpa")
+    """dvattn_sdpa through the C ABI (one prepared call)."""
+    SdpaCall(out, scale, locations, queries, fragment_lengths, keys, values, lse=lse, out_f32=out_f32)()
     return out
+
+
+def paged_append(k_cache, v_cache, keys, values, cosines, sines, block_tables, positions, counts=None):
+    """dvattn_paged_append through the C ABI: keys/values [W,Hkv,n,E|Ev] (keys unrotated),
+    cosines/sines [W,n,R] f32, positions [W] i32, counts [W] i32 or None."""
+    W, Hkv, n, E = keys.shape
+    NB, BS = k_cache.shape[:2]
+    a = AppendArgs(_DTYPE.get(k_cache.dtype, -1), W, Hkv, E, values.size(3), n, cosines.size(2), BS,
+                   block_tables.size(1), NB, k_cache.data_ptr(), v_cache.data_ptr(), keys.data_ptr(),
+                   values.data_ptr(), _ptr(cosines), _ptr(sines), block_tables.data_ptr(), positions.data_ptr(),
+                   _ptr(counts))
+    st = lib().dvattn_paged_append(ctypes.byref(a), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_paged_append")
+
+
+def build_views(locations, cosines, sines, seg_lengths, seg_order, rope_base, attention_scaling=1.0,
+                round_dtype=DVATTN_FLOAT32, inv_freq=None):
+    """dvattn_build_views through the C ABI: locations [F,W,n] i32, cosines/sines [F,W,n,R] f32
+    (written), seg_lengths [F] i32, seg_order [W,F] i32, inv_freq [R/2] f32 or None."""
+    F, W, n = locations.shape
+    a = ViewsArgs(F, W, n, cosines.size(3), float(rope_base), float(attention_scaling), round_dtype,
+                  seg_lengths.data_ptr(), seg_order.data_ptr(), _ptr(inv_freq), locations.data_ptr(),
+                  _ptr(cosines), _ptr(sines))
+    st = lib().dvattn_build_views(ctypes.byref(a), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_build_views")

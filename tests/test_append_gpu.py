@@ -8,6 +8,7 @@ import torch
 import fixtures
 import dvattn_b200
 from conftest import assert_lse_close, assert_out_close
+from dvattn_b200 import capi
 from dvattn_b200 import workloads as wl
 from oracle import dvattn_oracle as O
 
@@ -33,8 +34,11 @@ def test_append_golden_rotation(name):
     assert torch.equal(vc.reshape(W, maxb * BS, Hkv, E)[:, :n].permute(0, 2, 1, 3).cpu(), t["keys"])
 
 
-@pytest.mark.parametrize("dtype,E,R", [(torch.bfloat16, 128, 64), (torch.float16, 256, 128), (torch.float32, 64, 0)])
-def test_append_random_vs_oracle(dtype, E, R):
+# R = 24 (bf16) and R = 12 (f32) put a rotary half boundary inside a 16-byte chunk
+@pytest.mark.parametrize("dtype,E,R", [(torch.bfloat16, 128, 64), (torch.float16, 256, 128), (torch.float32, 64, 0),
+                                       (torch.bfloat16, 128, 24), (torch.float32, 64, 12), (torch.float32, 128, 32)])
+@pytest.mark.parametrize("via", ["op", "capi"])
+def test_append_random_vs_oracle(dtype, E, R, via):
     rs = np.random.RandomState(E + R)
     W, Hkv, n, BS, maxb = 5, 2, 37, 16, 12
     NB = W * maxb
@@ -52,8 +56,8 @@ def test_append_random_vs_oracle(dtype, E, R):
     counts = torch.from_numpy(np.array([n, 0, 11, n - 3, 20], np.int32))
     ek, ev = O.paged_append(kc, vc, keys, vals, cos, sin, bt, pos, counts)
     dk, dv = kc.to(DEV), vc.to(DEV)
-    dvattn_b200.dvattn_paged_append(dk, dv, keys.to(DEV), vals.to(DEV), cos.to(DEV), sin.to(DEV), bt.to(DEV),
-                                    pos.to(DEV), counts.to(DEV))
+    fn = dvattn_b200.dvattn_paged_append if via == "op" else capi.paged_append
+    fn(dk, dv, keys.to(DEV), vals.to(DEV), cos.to(DEV), sin.to(DEV), bt.to(DEV), pos.to(DEV), counts.to(DEV))
     torch.cuda.synchronize()
     assert torch.equal(dk.cpu(), ek)
     assert torch.equal(dv.cpu(), ev)

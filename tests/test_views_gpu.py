@@ -64,3 +64,25 @@ def test_views_golden(name):
     tol = 2e-5 if dt == torch.float32 else 8e-3
     torch.testing.assert_close(cos.cpu(), t["cosines"], rtol=0, atol=tol)
     torch.testing.assert_close(sin.cpu(), t["sines"], rtol=0, atol=tol)
+
+
+def test_views_capi_matches_op():
+    """The C ABI entry point writes what the torch op writes (and with no inv_freq, the
+    device computes 1/base^(2j/R) itself, equal to the host's within f32 rounding)."""
+    from dvattn_b200 import capi
+    rs = np.random.RandomState(8)
+    F, W, n, R = 3, 4, 7, 128
+    lens = torch.from_numpy(rs.randint(n, 5000, size=F).astype(np.int32)).to(DEV)
+    order = torch.from_numpy(np.stack([rs.permutation(F) for _ in range(W)]).astype(np.int32)).to(DEV)
+    loc, cos, sin = dvattn_b200.dvattn_build_views(lens, order, n, R, 500000.0, 1.0, torch.bfloat16)
+    inv = (1.0 / (500000.0 ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))).to(DEV)
+    for iv in (inv, None):
+        l2, c2, s2 = torch.empty_like(loc), torch.empty_like(cos), torch.empty_like(sin)
+        capi.build_views(l2, c2, s2, lens, order, 500000.0, 1.0, capi.DVATTN_BFLOAT16, inv_freq=iv)
+        torch.cuda.synchronize()
+        assert torch.equal(l2, loc)
+        if iv is not None:
+            assert torch.equal(c2, cos) and torch.equal(s2, sin)
+        else:
+            torch.testing.assert_close(c2, cos, rtol=0, atol=8e-3)
+            torch.testing.assert_close(s2, sin, rtol=0, atol=8e-3)
