@@ -667,7 +667,7 @@ def run_sdpa(args, world, rank, local):
             "config": {"workload": "sdpa2: config 2 on dvattn_sdpa, 2 turns of fragments [32, 4, L_f, 128] bf16, "
                                    "64 query heads", "bytes_per_step_per_gpu": nbytes,
                        "parallelism": f"batch-replica x{world}", "l2": "3 rotating fragment sets (~2 GB each)"},
-            "roofline": {"bound": "hbm", "kernel": "decode_tc_kernel (fragment addressing) + merge",
+            "roofline": {"bound": "hbm", "kernel": "decode_row_kernel (5-D TMA fragment boxes) + merge",
                          "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4),
                          "timing": "whole call (schedule + attention + merge), back to back", "traffic": None},

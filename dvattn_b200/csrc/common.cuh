@@ -171,6 +171,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* map, int x
         "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
         : "memory");
 }
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* map, int x, int y, int z, int w, int v,
+                                            uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+        "%6}], [%7];" ::"r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v), "r"(bar)
+        : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

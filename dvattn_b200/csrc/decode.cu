@@ -14,6 +14,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -166,7 +167,7 @@ __device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, i
     for (int t = tid; t < nh * 16 * CH; t += nth) {
         const int row = t / CH, ch = t - row * CH;
         const int g = row & 15;
-        const T* q = static_cast<const T*>(p.q) +
+        const T* q = static_cast<const T*>(p.q) + (size_t)f * p.q_turn_stride +
                      (((size_t)w * p.Hq + (row >> 4) * p.gqa + (g < p.gqa ? g : 0)) * p.S + s) * E + ch * 8;
         cp_async16_zfill(smem_u32(slot(row, ch)), q, g < p.gqa ? 16 : 0);
     }
@@ -207,12 +208,13 @@ __device__ __forceinline__ void prefetch_rotation_inputs(const PagedParams& p, i
     const int w = ws / p.S, s = ws - w * p.S;
     if (p.S == 1) {
         // the row's q block (Hq * E elements, contiguous): one L2 prefetch per 128-B line
-        const char* q = reinterpret_cast<const char*>(static_cast<const T*>(p.q) + (size_t)w * p.Hq * E);
+        const char* q = reinterpret_cast<const char*>(static_cast<const T*>(p.q) + (size_t)f * p.q_turn_stride +
+                                                      (size_t)w * p.Hq * E);
         const int lines = (int)((p.Hq * E * sizeof(T) + 127) / 128);
         for (int i = lane; i < lines; i += 32) asm volatile("prefetch.global.L2 [%0];" ::"l"(q + (size_t)i * 128));
     } else {
         for (int hq = lane; hq < p.Hq; hq += 32) {
-            const T* q = static_cast<const T*>(p.q) + (((size_t)w * p.Hq + hq) * p.S + s) * E;
+            const T* q = static_cast<const T*>(p.q) + (size_t)f * p.q_turn_stride + (((size_t)w * p.Hq + hq) * p.S + s) * E;
             asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(q), "r"((uint32_t)(E * sizeof(T))) : "memory");
         }
     }
@@ -993,6 +995,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         if (lane == 0 && c == 0) {
             p.sched->U = U;
             p.sched->n_eff = n;
+            // cleared once per call; a bounded wait sets a bit only after it has run out
+            // (long after every CTA passed griddepcontrol.wait), so the clear comes first
+            p.sched->error = 0;
         }
     };
     if (p.fused) {
@@ -1037,7 +1042,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
 
     if (wid == CW) {
         // =========================== producer warp ===========================
-        if (lane == 0) {
+        if (lane == 0 && !p.nfrag) {
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
         }
@@ -1054,6 +1059,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         auto prep = [&](Pend& q) {
             q.have = it.next(p, q.d);
             if (!q.have) return;
+            if (p.nfrag) {  // contiguous fragment: one box per window, no block table
+                q.pfirst = 0;
+                q.npg = 1;
+                q.page = __ldg(&p.frag[q.d.f].wmul);  // batch multiplier, loaded a tile ahead
+                if (q.d.new_turn) prefetch_rotation_inputs<T, E>(p, q.d.ws, q.d.f, lane);
+                return;
+            }
             const int pos0 = q.d.pos0;
             if (p.BS <= TOKB) {
                 const int last = pos0 + q.d.n - 1;
@@ -1104,6 +1116,18 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                 mbar_expect_tx(bar_full + st * 8, (uint32_t)cur.npg * 2u * box_bytes);
             }
             __syncwarp();
+            if (p.nfrag) {
+                // rows [win - off, win - off + TOKB) of turn f's fragment (rows outside it
+                // read as zeros), batch entry w (or 0 for a fragment all workers share)
+                if (lane == 0) {
+                    const int b = (p.S == 1 ? d.ws : d.ws / p.S) * cur.page;
+                    const char* mk = p.fmaps + (size_t)d.f * 256;
+                    const uint32_t off = (uint32_t)(st * C::STAGE_BYTES);
+                    tma_load_5d(sK0 + off, mk, 0, win - d.off, 0, 0, b, bar_full + st * 8);
+                    tma_load_5d(sV0 + off, mk + 128, 0, win - d.off, 0, 0, b, bar_full + st * 8);
+                }
+                continue;
+            }
             if (lane < cur.npg) {
                 const int page = cur.page;
                 const bool valid = p.NB <= 0 || (page >= 0 && page < p.NB);
@@ -1924,7 +1948,7 @@ static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
 }
 
 struct DecodeLayout {
-    size_t off_P, off_rs, off_cs, off_po, off_pl, off_fd, total;
+    size_t off_P, off_rs, off_cs, off_po, off_pl, off_fd, off_fm, total;
 };
 static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int slot_heads, int nfrag = 0) {
     auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
@@ -1935,13 +1959,27 @@ static DecodeLayout decode_layout(int WS, int E, int n_launch, bool varlen, int 
     L.off_po = L.off_cs + up(sizeof(long long) * (size_t)(n_launch + 1));
     L.off_pl = L.off_po + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16 * E);
     L.off_fd = L.off_pl + up(sizeof(float) * (size_t)n_launch * 2 * slot_heads * 16);
-    L.total = L.off_fd + up(sizeof(FragDesc) * (size_t)nfrag);
+    L.off_fm = L.off_fd + up(sizeof(FragDesc) * (size_t)nfrag);
+    L.total = L.off_fm + (size_t)nfrag * 256;  // K and V tensor maps of each fragment (row kernel)
     return L;
 }
 
 static bool choose(int dtype, int E, int Hkv, int BS, long long NB, KernelChoice& kc) {
     if (pick_row(dtype, E, Hkv, BS, NB, kc)) return true;
     if (tma_eligible(dtype, BS, NB) && pick_tma(dtype, E, kc)) return true;
+    return pick_kernel(dtype, E, kc);
+}
+
+// Contiguous fragments: the row kernel with one 5-D TMA box per window where it applies
+// (16-bit types, Hkv in {1, 2, 4, 8}); the cp.async kernels otherwise.
+// DVATTN_SDPA_ROW=0 keeps every call on the cp.async kernels.
+// Every fragment needs at least one row for its tensor map (an empty one goes the cp.async way).
+static bool choose_sdpa(int dtype, int E, int Hkv, bool all_rows, KernelChoice& kc) {
+    const char* env = getenv("DVATTN_SDPA_ROW");
+    if (all_rows && !(env && env[0] == '0')) {
+        const int tokb = 16 * (Hkv == 8 ? 8 : 4) / (Hkv > 0 ? Hkv : 1);
+        if (pick_row(dtype, E, Hkv, tokb, 1, kc)) return true;
+    }
     return pick_kernel(dtype, E, kc);
 }
 
@@ -1958,8 +1996,9 @@ size_t decode_workspace_size(const dvattn_paged_args* a) {
 // cs_stride, cu_q/nseq); fills the workspace-derived fields.
 static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
     KernelChoice kc;
-    // contiguous fragments: the cp.async kernels (per-row addresses), not the TMA ones
-    if (p.nfrag ? !pick_kernel(dtype, p.E, kc) : !choose(dtype, p.E, p.Hkv, p.BS, p.NB, kc))
+    bool all_rows = true;
+    for (int f = 0; f < p.nfrag; ++f) all_rows = all_rows && p.frag[f].rows > 0;
+    if (p.nfrag ? !choose_sdpa(dtype, p.E, p.Hkv, all_rows, kc) : !choose(dtype, p.E, p.Hkv, p.BS, p.NB, kc))
         return DVATTN_ERR_UNSUPPORTED;
     int n_launch = 0;
     int st = device_sms_and_occ(kc, n_launch);
@@ -1977,13 +2016,30 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.part_lse = reinterpret_cast<float*>(wsb + L.off_pl);
     p.cstart = reinterpret_cast<long long*>(wsb + L.off_cs);
     if (p.nfrag) {
-        // the fragment descriptors travel in the workspace (staged from the host array)
+        // the fragment descriptors (and, for the row kernel, each fragment's K and V tensor
+        // maps) travel in the workspace: one copy from a host staging array
         if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) {
-            if (cudaMemcpyAsync(wsb + L.off_fd, p.frag, sizeof(FragDesc) * (size_t)p.nfrag, cudaMemcpyHostToDevice,
-                                stream) != cudaSuccess)
+            std::vector<unsigned char> stage(L.total - L.off_fd, 0);
+            memcpy(stage.data(), p.frag, sizeof(FragDesc) * (size_t)p.nfrag);
+            size_t n = sizeof(FragDesc) * (size_t)p.nfrag;
+            if (kc.row) {
+                const int boxr = 16 * kc.cw / p.Hkv;
+                for (int f = 0; f < p.nfrag; ++f) {
+                    const FragDesc& fd = p.frag[f];
+                    alignas(64) CUtensorMap m[2];
+                    const int B = fd.wmul ? p.W : 1;
+                    if (!encode_fragment_map(&m[0], fd.k, dtype, p.E, p.Hkv, fd.rows, B, boxr) ||
+                        !encode_fragment_map(&m[1], fd.v, dtype, p.E, p.Hkv, fd.rows, B, boxr))
+                        return DVATTN_ERR_CUDA;
+                    memcpy(stage.data() + (L.off_fm - L.off_fd) + (size_t)f * 256, m, sizeof(m));
+                }
+                n = stage.size();
+            }
+            if (cudaMemcpyAsync(wsb + L.off_fd, stage.data(), n, cudaMemcpyHostToDevice, stream) != cudaSuccess)
                 return DVATTN_ERR_CUDA;
         }
         p.frag = reinterpret_cast<const FragDesc*>(wsb + L.off_fd);
+        p.fmaps = wsb + L.off_fm;
     }
     {
         // a query rotation costs about as long as streaming ~96 KB of the cache
@@ -2030,10 +2086,16 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
             alignas(64) CUtensorMap mk, mv;
             const int win = kc.row ? 16 * kc.cw / p.Hkv : 64;
             int boxr = p.BS < win ? p.BS : win;
-            const long long tokens = p.NB * p.BS;
-            auto enc = kc.row ? encode_cache_map_all_heads : encode_cache_map;
-            if (!enc(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) || !enc(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
-                return DVATTN_ERR_CUDA;
+            if (p.nfrag) {
+                boxr = win;  // one fragment box per window; the maps are in the workspace
+                memset(&mk, 0, sizeof(mk));
+                memset(&mv, 0, sizeof(mv));
+            } else {
+                const long long tokens = p.NB * p.BS;
+                auto enc = kc.row ? encode_cache_map_all_heads : encode_cache_map;
+                if (!enc(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) || !enc(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
+                    return DVATTN_ERR_CUDA;
+            }
             void* args[] = {&p, &mk, &mv, &boxr};
             if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;
         } else {
@@ -2192,10 +2254,12 @@ static int sdpa_validate(const dvattn_sdpa_args* a) {
 size_t sdpa_workspace_size(const dvattn_sdpa_args* a) {
     if (sdpa_validate(a) != DVATTN_OK) return 0;
     KernelChoice kc;
-    pick_kernel(a->dtype, a->E, kc);
+    bool all_rows = true;
+    for (int f = 0; f < a->F; ++f) all_rows = all_rows && a->fragment_rows[f] > 0;
+    choose_sdpa(a->dtype, a->E, a->Hkv, all_rows, kc);
     int n_launch = 0;
     if (device_sms_and_occ(kc, n_launch) != DVATTN_OK) return 0;
-    return decode_layout(a->W * a->S, a->E, n_launch, false, 1, a->F).total;
+    return decode_layout(a->W * a->S, a->E, n_launch, false, kc.row ? a->Hkv : 1, a->F).total;
 }
 
 int sdpa_launch(const dvattn_sdpa_args* a, void* workspace, size_t wbytes, cudaStream_t stream) {

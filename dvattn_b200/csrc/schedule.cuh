@@ -83,6 +83,9 @@ struct PagedParams {
     int nfrag;
     long long q_turn_stride;
     const FragDesc* frag;
+    // row kernel on fragments: 2 * nfrag 128-byte tensor maps (K then V of each turn) in
+    // the workspace
+    const char* fmaps;
 };
 
 

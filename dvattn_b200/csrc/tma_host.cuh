@@ -41,6 +41,25 @@ inline bool encode_cache_map_all_heads(CUtensorMap* m, const void* base, int dty
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Contiguous fragment [B][Hkv][rows][E] as a 5-D map whose box (64 columns x boxr rows x
+// all panels x all heads x 1 batch entry) lands in shared memory in the same
+// [head][panel][row][128 B] order as encode_cache_map_all_heads's page box.
+inline bool encode_fragment_map(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long rows, int B,
+                                int boxr) {
+    auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    const cuuint64_t r = rows > 0 ? (cuuint64_t)rows : 1;
+    cuuint64_t dims[5] = {64, r, (cuuint64_t)(E / 64), (cuuint64_t)Hkv, (cuuint64_t)(B > 0 ? B : 1)};
+    cuuint64_t strides[4] = {(cuuint64_t)E * 2, 128, r * E * 2, (cuuint64_t)Hkv * r * E * 2};
+    cuuint32_t box[5] = {64, (cuuint32_t)boxr, (cuuint32_t)(E / 64), (cuuint32_t)Hkv, 1};
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    const CUtensorMapDataType dt =
+        dtype == DVATTN_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    return fn(m, dt, 5, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 inline bool encode_cache_map(CUtensorMap* m, const void* base, int dtype, int E, int Hkv, long long tokens, int boxr) {
     auto fn = tensor_map_encoder();
     if (!fn) return false;

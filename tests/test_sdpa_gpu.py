@@ -111,3 +111,55 @@ def test_sdpa_errors():
         torch.ops.libdvatt.dvattn_sdpa(out.to(torch.float64), c.scale, c.locations, c.rotated.double(),
                                        c.fragment_lengths, [k.double() for k in c.keys],
                                        [v.double() for v in c.values])
+
+
+ROW_CASES = {
+    "bf16_hkv1_e128": dict(lens=[333, 1290], W=3, Hq=16, Hkv=1, E=128, R=0, dtype=torch.bfloat16, seed=51),
+    "f16_hkv2_e64_s2": dict(lens=[77, 501, 64], W=2, Hq=16, Hkv=2, E=64, R=0, dtype=torch.float16, seed=52, S=2),
+    "bf16_hkv4_e128_shared": dict(lens=[129, 1000], W=5, Hq=64, Hkv=4, E=128, R=0, dtype=torch.bfloat16, seed=53,
+                                  batch=1),
+    "bf16_hkv8_e128": dict(lens=[45, 700], W=2, Hq=64, Hkv=8, E=128, R=0, dtype=torch.bfloat16, seed=54),
+    "f16_hkv2_e256": dict(lens=[300, 17], W=2, Hq=32, Hkv=2, E=256, R=0, dtype=torch.float16, seed=55),
+    "bf16_3d_frag": dict(lens=[250, 90], W=1, Hq=16, Hkv=2, E=128, R=0, dtype=torch.bfloat16, seed=56, batch=None),
+}
+
+
+@pytest.mark.parametrize("name", sorted(ROW_CASES))
+def test_sdpa_tma_row_path(name, monkeypatch):
+    """16-bit fragments run on the TMA row kernel (one 5-D box per window); the cp.async
+    kernel (DVATTN_SDPA_ROW=0) and the oracle give the same result."""
+    c = wl.make_sdpa(**ROW_CASES[name])
+    g = c.to(DEV)
+    W, Hq, S, E = c.queries.shape
+    res = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("DVATTN_SDPA_ROW", mode)
+        out = torch.full((W, Hq, S, E), float("nan"), dtype=c.dtype, device=DEV)
+        lse = torch.full((W, Hq, S), float("nan"), device=DEV)
+        o32 = torch.full((W, Hq, S, E), float("nan"), device=DEV)
+        capi.sdpa(out, g.scale, g.locations, g.rotated, g.fragment_lengths, g.keys, g.values, lse=lse, out_f32=o32)
+        torch.cuda.synchronize()
+        res[mode] = (out, lse, o32)
+    ref, rlse = O.sdpa_pt(c.rotated, c.locations, c.keys, c.values, c.scale, return_lse=True)
+    out, lse, o32 = res["1"]
+    assert_out_close(out, ref.to(c.dtype), c.dtype, name)
+    assert_out_close(o32, ref, c.dtype, name + " f32")
+    assert_lse_close(lse, rlse, name)
+    # the two kernels split the keys differently, so P is rounded to 16 bits at different
+    # running maxima: agreement to the 16-bit rounding of P, not to the bit
+    torch.testing.assert_close(o32, res["0"][2], rtol=0, atol=4e-3)
+    torch.testing.assert_close(lse, res["0"][1], rtol=1e-5, atol=1e-5)
+
+
+def test_sdpa_rows_past_fragment_length(monkeypatch):
+    """Fragments with more rows than fragment_lengths (a preallocated buffer): only the
+    first L_f rows exist for the op."""
+    c = wl.make_sdpa([200, 150], W=2, Hq=32, Hkv=2, E=128, R=0, dtype=torch.bfloat16, seed=57)
+    g = c.to(DEV)
+    pad_k = [torch.cat((k, torch.randn_like(k[:, :, :37])), 2).contiguous() for k in g.keys]
+    pad_v = [torch.cat((v, torch.randn_like(v[:, :, :37])), 2).contiguous() for v in g.values]
+    out = torch.empty(tuple(c.queries.shape), dtype=c.dtype, device=DEV)
+    capi.sdpa(out, g.scale, g.locations, g.rotated, g.fragment_lengths, pad_k, pad_v)
+    torch.cuda.synchronize()
+    ref = O.sdpa_pt(c.rotated, c.locations, c.keys, c.values, c.scale)
+    assert_out_close(out, ref.to(c.dtype), c.dtype, "padded fragments")
