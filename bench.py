@@ -670,7 +670,8 @@ def run_sdpa(args, world, rank, local):
             "roofline": {"bound": "hbm", "kernel": "decode_row_kernel (5-D TMA fragment boxes) + merge",
                          "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4),
-                         "timing": "whole call (schedule + attention + merge), back to back", "traffic": None},
+                         "timing": "whole call (schedule + attention + merge), back to back",
+                         "traffic": traffic_from_profiles("sdpa2")},
             "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_ms * 1e3, 2),
                     "api": "torch.ops.libdvatt.dvattn_sdpa"},
@@ -761,7 +762,8 @@ def run_append(args, world, rank, local):
             "roofline": {"bound": "hbm", "kernel": "paged_append_kernel",
                          "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4), "traffic": None},
+                         "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                         "traffic": traffic_from_profiles("append4")},
             "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host), "d2h_bytes_per_step": 0,
                     "us_per_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_paged_append"},
