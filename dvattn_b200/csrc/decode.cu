@@ -947,10 +947,18 @@ struct RowCfg {
     static constexpr size_t SMEM = OFF_FLAG + 16;
 };
 
+// Tensor maps of up to kParamFrags contiguous fragments, passed by value to the row kernel
+// so that a dvattn_sdpa call needs no host-to-device copy (more fragments: the workspace).
+constexpr int kParamFrags = 4;
+struct alignas(64) FragMaps {
+    CUtensorMap m[2 * kParamFrags];  // K then V of each fragment
+    int wmul[kParamFrags];
+};
+
 template <class T, int E, int CW, int STAGES>
 __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     decode_row_kernel(PagedParams p, const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                      int boxr) {
+                      int boxr, const __grid_constant__ FragMaps fm) {
     using C = RowCfg<T, E, CW, STAGES>;
     constexpr int NPANEL = C::NPANEL;
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -1062,7 +1070,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             if (p.nfrag) {  // contiguous fragment: one box per window, no block table
                 q.pfirst = 0;
                 q.npg = 1;
-                q.page = __ldg(&p.frag[q.d.f].wmul);  // batch multiplier, loaded a tile ahead
+                // batch multiplier, loaded a tile ahead
+                q.page = p.fmaps ? __ldg(&p.frag[q.d.f].wmul) : fm.wmul[q.d.f];
                 if (q.d.new_turn) prefetch_rotation_inputs<T, E>(p, q.d.ws, q.d.f, lane);
                 return;
             }
@@ -1121,7 +1130,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                 // read as zeros), batch entry w (or 0 for a fragment all workers share)
                 if (lane == 0) {
                     const int b = (p.S == 1 ? d.ws : d.ws / p.S) * cur.page;
-                    const char* mk = p.fmaps + (size_t)d.f * 256;
+                    const char* mk = p.fmaps ? p.fmaps + (size_t)d.f * 256
+                                             : reinterpret_cast<const char*>(&fm.m[2 * d.f]);
                     const uint32_t off = (uint32_t)(st * C::STAGE_BYTES);
                     tma_load_5d(sK0 + off, mk, 0, win - d.off, 0, 0, b, bar_full + st * 8);
                     tma_load_5d(sV0 + off, mk + 128, 0, win - d.off, 0, 0, b, bar_full + st * 8);
@@ -2015,7 +2025,23 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.part_o = reinterpret_cast<float*>(wsb + L.off_po);
     p.part_lse = reinterpret_cast<float*>(wsb + L.off_pl);
     p.cstart = reinterpret_cast<long long*>(wsb + L.off_cs);
-    if (p.nfrag) {
+    alignas(64) FragMaps fm;
+    memset(&fm, 0, sizeof(fm));
+    if (p.nfrag && kc.row && p.nfrag <= kParamFrags) {
+        // few fragments: their tensor maps travel as a kernel parameter (no copy in the
+        // stream, so consecutive calls' kernels still overlap)
+        const int boxr = 16 * kc.cw / p.Hkv;
+        for (int f = 0; f < p.nfrag; ++f) {
+            const FragDesc& fd = p.frag[f];
+            const int B = fd.wmul ? p.W : 1;
+            if (!encode_fragment_map(&fm.m[2 * f], fd.k, dtype, p.E, p.Hkv, fd.rows, B, boxr) ||
+                !encode_fragment_map(&fm.m[2 * f + 1], fd.v, dtype, p.E, p.Hkv, fd.rows, B, boxr))
+                return DVATTN_ERR_CUDA;
+            fm.wmul[f] = fd.wmul;
+        }
+        p.frag = nullptr;
+        p.fmaps = nullptr;
+    } else if (p.nfrag) {
         // the fragment descriptors (and, for the row kernel, each fragment's K and V tensor
         // maps) travel in the workspace: one copy from a host staging array
         if (phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) {
@@ -2087,7 +2113,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
             const int win = kc.row ? 16 * kc.cw / p.Hkv : 64;
             int boxr = p.BS < win ? p.BS : win;
             if (p.nfrag) {
-                boxr = win;  // one fragment box per window; the maps are in the workspace
+                boxr = win;  // one fragment box per window; the maps are in fm or the workspace
                 memset(&mk, 0, sizeof(mk));
                 memset(&mv, 0, sizeof(mv));
             } else {
@@ -2096,8 +2122,13 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
                 if (!enc(&mk, p.k, dtype, p.E, p.Hkv, tokens, boxr) || !enc(&mv, p.v, dtype, p.E, p.Hkv, tokens, boxr))
                     return DVATTN_ERR_CUDA;
             }
-            void* args[] = {&p, &mk, &mv, &boxr};
-            if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;
+            if (kc.row) {
+                void* args[] = {&p, &mk, &mv, &boxr, &fm};
+                if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;
+            } else {
+                void* args[] = {&p, &mk, &mv, &boxr};
+                if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;
+            }
         } else {
             void* args[] = {&p};
             if (cudaLaunchKernelExC(&cfg, kc.fn, args) != cudaSuccess) return DVATTN_ERR_CUDA;

@@ -121,6 +121,9 @@ ROW_CASES = {
     "bf16_hkv8_e128": dict(lens=[45, 700], W=2, Hq=64, Hkv=8, E=128, R=0, dtype=torch.bfloat16, seed=54),
     "f16_hkv2_e256": dict(lens=[300, 17], W=2, Hq=32, Hkv=2, E=256, R=0, dtype=torch.float16, seed=55),
     "bf16_3d_frag": dict(lens=[250, 90], W=1, Hq=16, Hkv=2, E=128, R=0, dtype=torch.bfloat16, seed=56, batch=None),
+    # more fragments than travel as a kernel parameter: tensor maps staged in the workspace
+    "bf16_hkv2_6turns": dict(lens=[40, 300, 7, 129, 64, 513], W=3, Hq=32, Hkv=2, E=128, R=0, dtype=torch.bfloat16,
+                             seed=58),
 }
 
 
