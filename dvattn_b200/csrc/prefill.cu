@@ -92,8 +92,8 @@ __device__ __forceinline__ uint32_t idesc(bool bf16, int m, int n, bool b_mn_maj
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(id), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(id), "r"(accumulate)
         : "memory");
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -147,8 +147,8 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t id, uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b), "r"(id), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b), "r"(id), "r"(accumulate)
         : "memory");
 }
 // Packed f32x2 arithmetic (one instruction for two lanes of a 64-bit register pair) and a
@@ -256,10 +256,10 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(Params p) {
 
 // Scratch instrumentation: compiled only with -DPF_TRACE (never in the product build).
 #ifdef PF_TRACE
-__device__ unsigned long long g_pf_trace[256 * 16];
+__device__ unsigned long long g_pf_trace[256 * 32];
 #define PF_TR(i, slot) \
     do { \
-        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (i) < 256) g_pf_trace[(i) * 16 + (slot)] = clock64(); \
+        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (i) < 256) g_pf_trace[(i) * 32 + (slot)] = clock64(); \
     } while (0)
 }  // namespace pf
 }  // namespace dvb
@@ -273,6 +273,19 @@ namespace pf {
     do { \
     } while (0)
 #endif
+
+// Waits of the producer and MMA warps: a poll every ~100 ns instead of a tight try_wait
+// loop, so the two softmax warps on the same SM sub-partitions get the issue slots
+// (bounded like mbar_wait).
+__device__ __forceinline__ bool mbar_wait_lazy(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        __nanosleep(100);
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitNs) return false;
+    }
+}
 
 // ---- the prefill kernel ---------------------------------------------------------
 // Keys the item's tokens can see in turn f (the union of their visible ranges), by a
@@ -371,7 +384,6 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
     if (wid == WARP_PRODUCER) {
         // =============================== producer ===============================
         if (lane == 0) {
@@ -407,7 +419,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         while (vq.valid) {
             while (kq.valid && ik <= iv + 1) {
                 const int ks = ik % KSTAGES;
-                if (*sAbort || (ik >= KSTAGES && !mbar_wait(k_empty + 8 * ks, (ik / KSTAGES - 1) & 1))) {
+                if (*sAbort || (ik >= KSTAGES && !mbar_wait_lazy(k_empty + 8 * ks, (ik / KSTAGES - 1) & 1))) {
                     ok = false;
                     break;
                 }
@@ -418,10 +430,11 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             }
             if (!ok) break;
             const int vs = iv & 1;
-            if (*sAbort || (iv >= VSTAGES && !mbar_wait(v_empty + 8 * vs, ((iv >> 1) - 1) & 1))) {
+            if (*sAbort || (iv >= VSTAGES && !mbar_wait_lazy(v_empty + 8 * vs, ((iv >> 1) - 1) & 1))) {
                 ok = false;
                 break;
             }
+            PF_TR(iv, 11);
             load(vq, &tmv, s0 + (uint32_t)(OFF_V + vs * TILE), v_full + 8 * vs);
             vq.next(p, it, lane);
             ++iv;
@@ -435,14 +448,19 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         const uint32_t id_s = idesc(bf16, M, KT, false);
         const uint32_t id_o = idesc(bf16, M, E, true);
         // S_grp = Q_grp K^T over the 128 head dims (8 k-steps of 16)
+        // Shared-memory descriptors: the 14-bit start-address field (address >> 4; shared
+        // addresses stay below 256 KB, so no carry) advances by offset >> 4, so every MMA's
+        // operands are one add from three base descriptors computed once.
+        const uint64_t dq0 = sdesc(s0 + (uint32_t)OFF_Q, 16, 1024);
+        const uint64_t dk0 = sdesc(s0 + (uint32_t)OFF_K, 16, 1024);
+        const uint64_t dv0 = sdesc(s0 + (uint32_t)OFF_V, PANEL, 1024);
         auto issue_s = [&](int grp, int ks) {
+            const uint64_t a0 = dq0 + (uint64_t)((grp * TILE) >> 4), b0 = dk0 + (uint64_t)((ks * TILE) >> 4);
             if (lane == 0) {
 #pragma unroll
                 for (int kk = 0; kk < E / 16; ++kk) {
-                    const uint32_t ko = (uint32_t)((kk >> 2) * PANEL + (kk & 3) * 32);
-                    const uint64_t a = sdesc(s0 + (uint32_t)(OFF_Q + grp * TILE) + ko, 16, 1024);
-                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_K + ks * TILE) + ko, 16, 1024);
-                    umma(tmem + 128 * grp, a, b, id_s, kk > 0 ? 1u : 0u);
+                    const uint64_t ko = (uint64_t)(((kk >> 2) * PANEL + (kk & 3) * 32) >> 4);
+                    umma(tmem + 128 * grp, a0 + ko, b0 + ko, id_s, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(s_full + 8 * grp);
             }
@@ -450,12 +468,12 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         };
         // O_grp += P_grp V over the 128 keys; P is packed 2 per column over S_grp's columns
         auto issue_pv = [&](int grp, int vs, bool acc) {
+            const uint64_t b0 = dv0 + (uint64_t)((vs * TILE) >> 4);
+            const uint32_t d = tmem + 256 + 128 * grp, a = tmem + 128 * grp;
             if (lane == 0) {
 #pragma unroll
-                for (int kk = 0; kk < KT / 16; ++kk) {
-                    const uint64_t b = sdesc(s0 + (uint32_t)(OFF_V + vs * TILE + kk * 16 * 128), PANEL, 1024);
-                    umma_ts(tmem + 256 + 128 * grp, tmem + 128 * grp + 8 * kk, b, id_o, (acc || kk > 0) ? 1u : 0u);
-                }
+                for (int kk = 0; kk < KT / 16; ++kk)
+                    umma_ts(d, a + 8 * kk, b0 + (uint64_t)((kk * 16 * 128) >> 4), id_o, (acc || kk > 0) ? 1u : 0u);
             }
             __syncwarp();
         };
@@ -470,31 +488,36 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         for (; ts.valid; ts.next(p, it, lane), ++i) {
             const int ks = i % KSTAGES, vs = i & 1;
             const bool first = ts.first();
-            if (!mbar_wait(k_full + 8 * ks, (i / KSTAGES) & 1)) { ok = false; break; }
+            if (!mbar_wait_lazy(k_full + 8 * ks, (i / KSTAGES) & 1)) { ok = false; break; }
             PF_TR(i, 1);
-            if (first && !mbar_wait(q_ready, turn & 1)) { ok = false; break; }
+            if (first && !mbar_wait_lazy(q_ready, turn & 1)) { ok = false; break; }
             tc_fence_after();
             issue_s(0, ks);
+            PF_TR(i, 18);
             if (i > 0) {
-                if (!mbar_wait(p_full + 8, (i - 1) & 1)) { ok = false; break; }
+                if (!mbar_wait_lazy(p_full + 8, (i - 1) & 1)) { ok = false; break; }
                 PF_TR(i - 1, 2);
                 tc_fence_after();
                 issue_pv(1, vs ^ 1, i - 1 > 0);
                 commit(v_empty + 8 * (vs ^ 1));
+                PF_TR(i, 19);
             }
-            if (first && !mbar_wait(q_ready + 8, turn & 1)) { ok = false; break; }
+            if (first && !mbar_wait_lazy(q_ready + 8, turn & 1)) { ok = false; break; }
             tc_fence_after();
             issue_s(1, ks);
             commit(k_empty + 8 * ks);
-            if (!mbar_wait(v_full + 8 * vs, (i >> 1) & 1)) { ok = false; break; }
-            if (!mbar_wait(p_full, i & 1)) { ok = false; break; }
+            PF_TR(i, 20);
+            if (!mbar_wait_lazy(v_full + 8 * vs, (i >> 1) & 1)) { ok = false; break; }
+            PF_TR(i, 15);
+            if (!mbar_wait_lazy(p_full, i & 1)) { ok = false; break; }
             PF_TR(i, 3);
             tc_fence_after();
             issue_pv(0, vs, i > 0);
+            PF_TR(i, 16);
             if (first) ++turn;
         }
         if (ok && i > 0) {
-            if (mbar_wait(p_full + 8, (i - 1) & 1)) {
+            if (mbar_wait_lazy(p_full + 8, (i - 1) & 1)) {
                 tc_fence_after();
                 issue_pv(1, (i - 1) & 1, i - 1 > 0);
             } else {
