@@ -770,6 +770,100 @@ def run_append(args, world, rank, local):
             "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": None}), flush=True)
 
 
+def run_views(args, world, rank, local):
+    """Turn/view metadata builder (row f-2) on config 4's prefill shape: F = 4 cache
+    segments shared by 16 workers in per-worker orders, n = 2048 new tokens per worker,
+    rotary dim 32, theta 1e6, bf16 rounding.  Metric: HBM GB/s of the written locations
+    and cos/sin rows (the inputs are a few hundred bytes)."""
+    import dvattn_b200  # registers torch.ops.libdvatt
+    from oracle import dvattn_oracle as O  # CPU baseline leg only
+    dev = f"cuda:{local}"
+    hbm_peak, _, peak_kind = load_peaks()
+    rs = np.random.RandomState(5)
+    F, W, n, R, base = 4, 16, 2048, 32, 1000000.0
+    lens = torch.from_numpy(rs.randint(n, 16384, size=F).astype(np.int32)).to(dev)
+    order = torch.from_numpy(np.stack([rs.permutation(F) for _ in range(W)]).astype(np.int32)).to(dev)
+    loc = torch.empty((F, W, n), dtype=torch.int32, device=dev)
+    cos = torch.empty((F, W, n, R), dtype=torch.float32, device=dev)
+    sin = torch.empty_like(cos)
+    inv = (1.0 / (base ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))).to(dev)
+    nbytes = F * W * n * (4 + 2 * R * 4)
+
+    def step():
+        torch.ops.libdvatt.dvattn_build_views(loc, cos, sin, lens, order, inv, base, 1.0, 2)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(args.steps):
+            step()
+    graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.begin()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.end()
+    clocks = sampler.stop() if sampler else None
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    # end to end: segment lengths and orders from pinned host memory, the tables back
+    h_in = [lens.cpu().pin_memory(), order.cpu().pin_memory()]
+    d_in = [torch.empty_like(lens), torch.empty_like(order)]
+    h_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (loc, cos, sin)]
+    e0.record()
+    for _ in range(args.steps):
+        for h, d in zip(h_in, d_in):
+            d.copy_(h, non_blocking=True)
+        torch.ops.libdvatt.dvattn_build_views(loc, cos, sin, d_in[0], d_in[1], inv, base, 1.0, 2)
+        for h, d in zip(h_out, (loc, cos, sin)):
+            h.copy_(d, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    total = sum_over_ranks(float(nbytes), world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        lh, oh = lens.cpu().numpy(), order.cpu().numpy()
+        O.build_views(lh, oh, n, R, base, 1.0, torch.bfloat16)
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            O.build_views(lh, oh, n, R, base, 1.0, torch.bfloat16)
+        dt = (time.perf_counter() - t0) / reps
+        cpu = {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": "the whole workload (oracle restatement of DVAttnCache.update + the rotary module, torch on CPU)"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "turn/view metadata build HBM GB/s", "value": round(total / (t_ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t_ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "float32 (bf16-rounded cos/sin)", "data": "synthetic (seeded)",
+            "config": {"workload": "views4: 4 segments x 16 workers x 2048 new tokens, rotary dim 32, theta 1e6",
+                       "bytes_per_step_per_gpu": nbytes, "parallelism": f"batch-replica x{world}",
+                       "l2": "34 MB written per step (outputs rewritten each step)"},
+            "roofline": {"bound": "hbm", "kernel": "build_views_vec_kernel",
+                         "achieved": round(nbytes / (t_ms * 1e-3) / 1e9, 2), "peak": hbm_peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(nbytes / (t_ms * 1e-3) / 1e9 / hbm_peak, 4),
+                         "traffic": traffic_from_profiles("views4")},
+            "e2e": {"value": round(total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in h_in),
+                    "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in h_out),
+                    "us_per_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_build_views"},
+            "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": cpu}), flush=True)
+
+
 def run_long3(args, world, rank, local):
     """Config 3 with its KV split across the ranks (page-aligned chunks) and the partial
     outputs merged over NCCL (all-gather of f32 O + LSE, then the LSE-merge kernel)."""
@@ -820,7 +914,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config2",
-                    choices=["config1", "config2", "config3", "config4", "config5", "long3", "sdpa2", "append4"])
+                    choices=["config1", "config2", "config3", "config4", "config5", "long3", "sdpa2", "append4",
+                             "views4"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-cuda", action="store_true", help="reference arm: skip timing the reference CUDA op")
     args = ap.parse_args()
@@ -838,6 +933,8 @@ def main():
         run_sdpa(args, world, rank, local)
     elif args.workload == "append4":
         run_append(args, world, rank, local)
+    elif args.workload == "views4":
+        run_views(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
     if world > 1:

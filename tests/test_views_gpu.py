@@ -86,3 +86,21 @@ def test_views_capi_matches_op():
         else:
             torch.testing.assert_close(c2, cos, rtol=0, atol=8e-3)
             torch.testing.assert_close(s2, sin, rtol=0, atol=8e-3)
+
+
+@pytest.mark.parametrize("R", [0, 12, 24, 40])
+def test_views_rotary_dims(R):
+    """R/2 a multiple of 4 (R = 24, 40) takes the coalesced kernel, R = 12 the per-row one;
+    R = 0 writes locations only."""
+    rs = np.random.RandomState(R + 1)
+    F, W, n = 3, 5, 9
+    lens = rs.randint(n, 3000, size=F).astype(np.int32)
+    order = np.stack([rs.permutation(F) for _ in range(W)]).astype(np.int32)
+    loc, cos, sin = dvattn_b200.dvattn_build_views(torch.from_numpy(lens).to(DEV), torch.from_numpy(order).to(DEV),
+                                                   n, R, 10000.0, 0.5, torch.float16)
+    torch.cuda.synchronize()
+    eloc, ecos, esin = O.build_views(lens, order, n, R, 10000.0, 0.5, torch.float16)
+    assert torch.equal(loc.cpu(), eloc)
+    if R:
+        torch.testing.assert_close(cos.cpu(), ecos, rtol=0, atol=1e-3)
+        torch.testing.assert_close(sin.cpu(), esin, rtol=0, atol=1e-3)
