@@ -1224,11 +1224,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
 #pragma unroll
             for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
         }
-#ifdef DVB_EXP_NOROT
-        if (false) {
-#else
         if ((d.flags & 2) && i > 0) {
-#endif
 #ifdef DVB_TRACE
             const unsigned long long tr0 = global_ns();
             if (tid == 0) DVB_TADD(6, tr0);
@@ -1250,11 +1246,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
 #endif
         }
 
-#ifdef DVB_EXP_NOMATH
-        const int lo = 0, hi = 0;
-#else
         const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
-#endif
         const uint32_t kb = sK0 + st * C::STAGE_BYTES;
         const uint32_t vb = sV0 + st * C::STAGE_BYTES;
         if (hi > lo) {
