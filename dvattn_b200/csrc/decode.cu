@@ -22,7 +22,14 @@ namespace dvb {
 
 // Scratch instrumentation: compiled only with -DDVB_TRACE (never in the product build).
 #ifdef DVB_TRACE
-__device__ unsigned long long g_trace[8][4096];
+__device__ unsigned long long g_trace[12][4096];
+}  // namespace dvb
+extern "C" void dvb_trace_read(unsigned long long* h) { cudaMemcpyFromSymbol(h, dvb::g_trace, sizeof(dvb::g_trace)); }
+extern "C" void dvb_trace_clear() {
+    static unsigned long long z[12][4096];
+    cudaMemcpyToSymbol(dvb::g_trace, z, sizeof(z));
+}
+namespace dvb {
 #define DVB_TC(k) do { if (blockIdx.x < 4096) g_trace[k][blockIdx.x] = global_ns(); } while (0)
 #define DVB_TADD(k, v) do { if (blockIdx.x < 4096) atomicAdd(&g_trace[k][blockIdx.x], (unsigned long long)(v)); } while (0)
 #else
@@ -1762,8 +1769,10 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     constexpr int NTH = 16 * (E / 4);
     // launched as a programmatic dependent of the attention kernel: wait for its results
     // let the next call's schedule kernel start its (read-only) work now
+    if (threadIdx.x == 0) DVB_TC(8);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (threadIdx.x == 0) DVB_TC(9);
     const int tid = threadIdx.x;
     // The CTA boundaries are searched twice below: stage them in shared memory with one
     // round of parallel loads instead of a chain of dependent global loads.
@@ -1778,6 +1787,10 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     __shared__ int s_part[NTH];
     for (int g_seg = blockIdx.x; g_seg < p.WS * p.Hkv; g_seg += gridDim.x)
         merge_segment<T, E>(p, g_seg, cst, sch.n_eff, s_part);
+#ifdef DVB_TRACE
+    __syncthreads();
+    if (threadIdx.x == 0) DVB_TC(10);
+#endif
 }
 
 // ==================================================================================
