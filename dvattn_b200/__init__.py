@@ -35,9 +35,11 @@ from .api import (  # noqa: E402
     dvattn_lse_merge,
     dvattn_paged_append,
     dvattn_paged_sdpa,
+    dvattn_paged_sdpa_rope,
     dvattn_rope,
     dvattn_sdpa,
     dvattn_varlen_paged_sdpa,
+    dvattn_varlen_paged_sdpa_rope,
     dvattn_varlen_rope,
     rotate_half,
 )
@@ -49,9 +51,11 @@ __all__ = [
     "dvattn_lse_merge",
     "dvattn_paged_append",
     "dvattn_paged_sdpa",
+    "dvattn_paged_sdpa_rope",
     "dvattn_rope",
     "dvattn_sdpa",
     "dvattn_varlen_paged_sdpa",
+    "dvattn_varlen_paged_sdpa_rope",
     "dvattn_varlen_rope",
     "rotate_half",
 ]

@@ -95,13 +95,49 @@ def dvattn_build_views(seg_lengths: torch.Tensor, seg_order: torch.Tensor, n: in
     loc = torch.empty((F, W, n), dtype=torch.int32, device=dev)
     cos = torch.empty((F, W, n, R), dtype=torch.float32, device=dev)
     sin = torch.empty((F, W, n, R), dtype=torch.float32, device=dev)
-    # the inverse frequencies exactly as the model's rotary module computes them (on the host)
-    inv_freq = None
-    if R:
-        inv_freq = (1.0 / (rope_base ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))).to(dev)
+    inv_freq = _inv_freq(R, rope_base, dev)
     _ops.dvattn_build_views(loc, cos, sin, seg_lengths, seg_order, inv_freq, rope_base, attention_scaling,
                             _ROUND[dtype])
     return loc, cos, sin
+
+
+def _inv_freq(R: int, rope_base: float, device) -> Optional[torch.Tensor]:
+    """The inverse frequencies exactly as the model's rotary module computes them (host)."""
+    if not R:
+        return None
+    return (1.0 / (rope_base ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))).to(device)
+
+
+def dvattn_paged_sdpa_rope(queries: torch.Tensor, locations: torch.Tensor, fragment_lengths: torch.Tensor,
+                           k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor, scale: float,
+                           rotary_dim: int, rope_base: float, attention_scaling: float = 1.0,
+                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dvattn_paged_sdpa with the query rotation of turn f taken as the model's rotary
+    embedding at the query's own location loc[f, w, s] (what DVAttnCache.update passes,
+    attention.py:161-191), built on the device: no cosines/sines tensors."""
+    if out is None:
+        W, Hq, S, _ = queries.shape
+        out = torch.empty((W, Hq, S, v_cache.size(3)), dtype=queries.dtype, device=queries.device)
+    _ops.dvattn_paged_sdpa_rope(out, scale, locations, queries, fragment_lengths, k_cache, v_cache, block_tables,
+                                rotary_dim, rope_base, attention_scaling, _inv_freq(rotary_dim, rope_base, out.device))
+    return out
+
+
+def dvattn_varlen_paged_sdpa_rope(queries: torch.Tensor, locations: torch.Tensor, fragment_lengths: torch.Tensor,
+                                  k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                                  cu_seqlens_q: torch.Tensor, scale: float, rotary_dim: int, rope_base: float,
+                                  attention_scaling: float = 1.0, cu_seqlens_k: Optional[torch.Tensor] = None,
+                                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dvattn_varlen_paged_sdpa with the rotation tables built on the device from the
+    locations (token t of turn f rotated by the rotary embedding at loc[f, t])."""
+    if out is None:
+        T, Hq, _ = queries.shape
+        out = torch.empty((T, Hq, v_cache.size(3)), dtype=queries.dtype, device=queries.device)
+    _ops.dvattn_varlen_paged_sdpa_rope(out, scale, locations, queries, fragment_lengths, k_cache, v_cache,
+                                       block_tables, cu_seqlens_q,
+                                       cu_seqlens_k if cu_seqlens_k is not None else cu_seqlens_q, rotary_dim,
+                                       rope_base, attention_scaling, _inv_freq(rotary_dim, rope_base, out.device))
+    return out
 
 
 def dvattn_paged_append(k_cache: torch.Tensor, v_cache: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,

@@ -52,6 +52,10 @@ EXPORTS = [
     "dvattn_sdpa",
     "dvattn_paged_append",
     "dvattn_build_views",
+    "dvattn_paged_sdpa_rope_workspace_size",
+    "dvattn_paged_sdpa_rope",
+    "dvattn_varlen_paged_sdpa_rope_workspace_size",
+    "dvattn_varlen_paged_sdpa_rope",
 ]
 
 _vp = ctypes.c_void_p
@@ -96,6 +100,11 @@ class ViewsArgs(ctypes.Structure):
                 ("seg_order", _vp), ("inv_freq", _vp), ("locations", _vp), ("cosines", _vp), ("sines", _vp)]
 
 
+class RotaryArgs(ctypes.Structure):
+    _fields_ = [("rope_base", ctypes.c_float), ("attention_scaling", ctypes.c_float), ("round_dtype", _i),
+                ("inv_freq", _vp)]
+
+
 _lib: Optional[ctypes.CDLL] = None
 
 
@@ -137,6 +146,16 @@ def lib() -> ctypes.CDLL:
         L.dvattn_lse_merge.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp, _vp]
         L.dvattn_paged_append.restype = _i
         L.dvattn_paged_append.argtypes = [ctypes.POINTER(AppendArgs), _vp]
+        L.dvattn_paged_sdpa_rope_workspace_size.restype = ctypes.c_size_t
+        L.dvattn_paged_sdpa_rope_workspace_size.argtypes = [ctypes.POINTER(PagedArgs), ctypes.POINTER(RotaryArgs)]
+        L.dvattn_paged_sdpa_rope.restype = _i
+        L.dvattn_paged_sdpa_rope.argtypes = [ctypes.POINTER(PagedArgs), ctypes.POINTER(RotaryArgs), _vp, ctypes.c_size_t,
+                                             _vp]
+        L.dvattn_varlen_paged_sdpa_rope_workspace_size.restype = ctypes.c_size_t
+        L.dvattn_varlen_paged_sdpa_rope_workspace_size.argtypes = [ctypes.POINTER(VarlenArgs), ctypes.POINTER(RotaryArgs)]
+        L.dvattn_varlen_paged_sdpa_rope.restype = _i
+        L.dvattn_varlen_paged_sdpa_rope.argtypes = [ctypes.POINTER(VarlenArgs), ctypes.POINTER(RotaryArgs), _vp,
+                                                    ctypes.c_size_t, _vp]
         L.dvattn_build_views.restype = _i
         L.dvattn_build_views.argtypes = [ctypes.POINTER(ViewsArgs), _vp]
         _lib = L
@@ -361,3 +380,40 @@ def build_views(locations, cosines, sines, seg_lengths, seg_order, rope_base, at
     st = lib().dvattn_build_views(ctypes.byref(a), _stream(None))
     if st != DVATTN_OK:
         raise DvattnError(st, "dvattn_build_views")
+
+
+def paged_sdpa_rope(out, scale, locations, queries, fragment_lengths, k_cache, v_cache, block_tables, rotary_dim,
+                    rope_base, attention_scaling=1.0, inv_freq=None, lse=None, out_f32=None):
+    """dvattn_paged_sdpa_rope through the C ABI (rotation tables built on the device from
+    the locations; cos/sin rounded through the output dtype)."""
+    dummy = torch.empty((locations.size(0), out.size(0), out.size(2), rotary_dim), device=out.device)
+    a = paged_args(out, scale, locations, queries, dummy, dummy, fragment_lengths, k_cache, v_cache, block_tables,
+                   lse=lse, out_f32=out_f32)
+    a.cosines = None
+    a.sines = None
+    r = RotaryArgs(float(rope_base), float(attention_scaling), _DTYPE.get(out.dtype, -1), _ptr(inv_freq))
+    n = lib().dvattn_paged_sdpa_rope_workspace_size(ctypes.byref(a), ctypes.byref(r))
+    ws = torch.empty(max(n, 256), dtype=torch.uint8, device=out.device)
+    st = lib().dvattn_paged_sdpa_rope(ctypes.byref(a), ctypes.byref(r), ws.data_ptr(), ws.numel(), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_paged_sdpa_rope")
+    return out
+
+
+def varlen_paged_sdpa_rope(out, scale, locations, queries, fragment_lengths, k_cache, v_cache, block_tables,
+                           cu_seqlens_q, rotary_dim, rope_base, attention_scaling=1.0, inv_freq=None, lse=None,
+                           out_f32=None):
+    """dvattn_varlen_paged_sdpa_rope through the C ABI."""
+    dummy = torch.empty((locations.size(0), queries.size(0), rotary_dim // 2), device=out.device)
+    a = varlen_args(out, scale, locations, queries, dummy, dummy, fragment_lengths, k_cache, v_cache, block_tables,
+                    cu_seqlens_q, lse=lse, out_f32=out_f32)
+    a.cosines = None
+    a.sines = None
+    r = RotaryArgs(float(rope_base), float(attention_scaling), _DTYPE.get(out.dtype, -1), _ptr(inv_freq))
+    n = lib().dvattn_varlen_paged_sdpa_rope_workspace_size(ctypes.byref(a), ctypes.byref(r))
+    ws = torch.empty(max(n, 256), dtype=torch.uint8, device=out.device)
+    st = lib().dvattn_varlen_paged_sdpa_rope(ctypes.byref(a), ctypes.byref(r), ws.data_ptr(), ws.numel(),
+                                             _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_varlen_paged_sdpa_rope")
+    return out

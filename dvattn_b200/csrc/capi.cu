@@ -35,6 +35,25 @@ int dvattn_varlen_paged_sdpa(const dvattn_varlen_args* args, void* workspace, si
     return dvb::varlen_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), DVATTN_PHASE_ALL);
 }
 
+size_t dvattn_paged_sdpa_rope_workspace_size(const dvattn_paged_args* args, const dvattn_rotary_args* rotary) {
+    return dvb::paged_rope_workspace_size(args, rotary);
+}
+
+int dvattn_paged_sdpa_rope(const dvattn_paged_args* args, const dvattn_rotary_args* rotary, void* workspace,
+                           size_t workspace_bytes, dvattn_stream_t stream) {
+    return dvb::paged_rope_launch(args, rotary, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t dvattn_varlen_paged_sdpa_rope_workspace_size(const dvattn_varlen_args* args, const dvattn_rotary_args* rotary) {
+    return dvb::varlen_rope_workspace_size(args, rotary);
+}
+
+int dvattn_varlen_paged_sdpa_rope(const dvattn_varlen_args* args, const dvattn_rotary_args* rotary, void* workspace,
+                                  size_t workspace_bytes, dvattn_stream_t stream) {
+    return dvb::varlen_rope_attn_launch(args, rotary, workspace, workspace_bytes,
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
 int dvattn_build_views(const dvattn_views_args* args, dvattn_stream_t stream) {
     return dvb::build_views_launch(args, reinterpret_cast<cudaStream_t>(stream));
 }

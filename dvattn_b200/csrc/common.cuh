@@ -218,4 +218,27 @@ __device__ __forceinline__ int visible_len(int L, int loc) {
     return v > 0 ? v : 0;
 }
 
+// ----------------------------------------------------------------------------------
+// The model's default rotary embedding at one position (HF rotary module): inv_freq_j =
+// 1 / base^(2j / R) in f32 (or the module's own table), freq = inv_freq_j * pos (one
+// rounding), cos/sin times attention_scaling, returned in the model dtype (round_dtype,
+// DVATTN_*) and widened to f32.  Shared by the view builder and the rope-table kernel so
+// both give the same bits.
+// ----------------------------------------------------------------------------------
+__device__ __forceinline__ void rotary_cos_sin(const float* inv_freq, float base, int R, int j, float pos,
+                                               float scaling, int round_dtype, float& c, float& s) {
+    const float inv = inv_freq ? __ldg(inv_freq + j) : 1.0f / powf(base, (float)(2 * j) / (float)R);
+    const float ang = __fmul_rn(inv, pos);
+    sincosf(ang, &s, &c);  // one argument reduction for both
+    c *= scaling;
+    s *= scaling;
+    if (round_dtype == DVATTN_BFLOAT16) {
+        c = Elem<__nv_bfloat16>::to_f(Elem<__nv_bfloat16>::from_f(c));
+        s = Elem<__nv_bfloat16>::to_f(Elem<__nv_bfloat16>::from_f(s));
+    } else if (round_dtype == DVATTN_FLOAT16) {
+        c = Elem<__half>::to_f(Elem<__half>::from_f(c));
+        s = Elem<__half>::to_f(Elem<__half>::from_f(s));
+    }
+}
+
 }  // namespace dvb

@@ -14,6 +14,13 @@ size_t varlen_workspace_size(const dvattn_varlen_args* a);
 int varlen_launch(const dvattn_varlen_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
 // turn/view metadata (views.cu)
 int build_views_launch(const dvattn_views_args* a, cudaStream_t stream);
+// attention with the rotary tables computed on the device from the locations (rope_tables.cu)
+size_t paged_rope_workspace_size(const dvattn_paged_args* a, const dvattn_rotary_args* r);
+int paged_rope_launch(const dvattn_paged_args* a, const dvattn_rotary_args* r, void* workspace, size_t wbytes,
+                      cudaStream_t stream);
+size_t varlen_rope_workspace_size(const dvattn_varlen_args* a, const dvattn_rotary_args* r);
+int varlen_rope_attn_launch(const dvattn_varlen_args* a, const dvattn_rotary_args* r, void* workspace, size_t wbytes,
+                            cudaStream_t stream);
 // paged KV append with fused K rotation (append.cu)
 int paged_append_launch(const dvattn_append_args* a, cudaStream_t stream);
 // contiguous fragments (the dvattn_sdpa op)

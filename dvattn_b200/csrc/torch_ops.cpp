@@ -51,19 +51,43 @@ dvattn_stream_t cur_stream(const at::Tensor& out) {
 // ---------------------------------------------------------------------------------
 // dvattn_paged_sdpa (src/binding.cu:151-203 / 312-325)
 // ---------------------------------------------------------------------------------
+// Rotary parameters of the *_rope ops (cos/sin tables built on the device from the
+// locations); null for the ops that take cosines/sines.
+struct RotaryOpt {
+    int R;
+    double base, scaling;
+    const c10::optional<at::Tensor>* inv_freq;
+};
+
+dvattn_rotary_args rotary_args(const RotaryOpt& r, const at::Tensor& out, int round_dtype) {
+    dvattn_rotary_args ra{};
+    ra.rope_base = static_cast<float>(r.base);
+    ra.attention_scaling = static_cast<float>(r.scaling);
+    ra.round_dtype = round_dtype;
+    TORCH_CHECK(r.R >= 0 && r.R % 2 == 0, "dvattn rope: rotary_dim must be even and >= 0");
+    if (r.inv_freq && r.inv_freq->has_value()) {
+        const at::Tensor& t = **r.inv_freq;
+        check_cuda_tensor(t, "inv_freq", out);
+        TORCH_CHECK(t.scalar_type() == at::kFloat && t.numel() == r.R / 2, "dvattn rope: inv_freq must be f32 [rotary_dim/2]");
+        ra.inv_freq = t.const_data_ptr<float>();
+    }
+    return ra;
+}
+
 void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
                 const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& fragment_lengths,
                 const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& block_tables,
-                const c10::optional<at::Tensor>& lse, const c10::optional<at::Tensor>& out_f32) {
+                const c10::optional<at::Tensor>& lse, const c10::optional<at::Tensor>& out_f32,
+                const RotaryOpt* rot = nullptr) {
     const c10::cuda::CUDAGuard guard(out.device());
     const int dt = dtype_code(out);
     TORCH_CHECK(out.dim() == 4, "dvattn_paged_sdpa: output must be [W, Hq, S, Ev]");
-    TORCH_CHECK(queries.dim() == 4 && locations.dim() == 3 && cosines.dim() == 4 && sines.dim() == 4 &&
+    TORCH_CHECK(queries.dim() == 4 && locations.dim() == 3 && (rot || (cosines.dim() == 4 && sines.dim() == 4)) &&
                     k_cache.dim() == 4 && v_cache.dim() == 4 && block_tables.dim() == 2 && fragment_lengths.dim() == 1,
                 "dvattn_paged_sdpa: wrong tensor ranks");
     for (auto* pr : {&queries, &k_cache, &v_cache})
         TORCH_CHECK(pr->scalar_type() == out.scalar_type(), "dvattn_paged_sdpa: queries/k_cache/v_cache must have the output dtype");
-    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat,
+    TORCH_CHECK(rot || (cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat),
                 "dvattn_paged_sdpa: cosines/sines must be float32");
     check_i32(locations, "locations");
     check_i32(fragment_lengths, "fragment_lengths");
@@ -71,8 +95,10 @@ void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, cons
     check_cuda_tensor(out, "output", out);
     check_cuda_tensor(queries, "queries", out);
     check_cuda_tensor(locations, "locations", out);
-    check_cuda_tensor(cosines, "cosines", out);
-    check_cuda_tensor(sines, "sines", out);
+    if (!rot) {
+        check_cuda_tensor(cosines, "cosines", out);
+        check_cuda_tensor(sines, "sines", out);
+    }
     check_cuda_tensor(fragment_lengths, "fragment_lengths", out);
     check_cuda_tensor(k_cache, "k_cache", out);
     check_cuda_tensor(v_cache, "v_cache", out);
@@ -84,9 +110,12 @@ void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, cons
     TORCH_CHECK(queries.size(0) == W && queries.size(1) == Hq && queries.size(2) == S,
                 "dvattn_paged_sdpa: queries must be [W, Hq, S, E]");
     const int E = queries.size(3);
-    const int R = cosines.size(3);
-    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == W && cosines.size(2) == S, "dvattn_paged_sdpa: cosines must be [F, W, S, R]");
-    TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_paged_sdpa: sines must match cosines");
+    const int R = rot ? rot->R : cosines.size(3);
+    if (!rot) {
+        TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == W && cosines.size(2) == S,
+                    "dvattn_paged_sdpa: cosines must be [F, W, S, R]");
+        TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_paged_sdpa: sines must match cosines");
+    }
     TORCH_CHECK(fragment_lengths.size(0) == F, "dvattn_paged_sdpa: fragment_lengths must be [F]");
     const int BS = k_cache.size(1), Hkv = k_cache.size(2);
     TORCH_CHECK(k_cache.size(3) == E, "dvattn_paged_sdpa: k_cache must be [NB, BS, Hkv, E]");
@@ -103,8 +132,8 @@ void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, cons
     a.scale = static_cast<float>(scale);
     a.out = out.data_ptr();
     a.queries = queries.const_data_ptr();
-    a.cosines = cosines.const_data_ptr<float>();
-    a.sines = sines.const_data_ptr<float>();
+    a.cosines = rot ? nullptr : cosines.const_data_ptr<float>();
+    a.sines = rot ? nullptr : sines.const_data_ptr<float>();
     a.locations = locations.const_data_ptr<int>();
     a.fragment_lengths = fragment_lengths.const_data_ptr<int>();
     a.k_cache = k_cache.const_data_ptr();
@@ -119,6 +148,14 @@ void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, cons
         check_cuda_tensor(*out_f32, "out_f32", out);
         TORCH_CHECK(out_f32->scalar_type() == at::kFloat && out_f32->numel() == out.numel(), "dvattn: out_f32 must be f32 like output");
         a.out_f32 = out_f32->data_ptr<float>();
+    }
+    if (rot) {
+        const dvattn_rotary_args ra = rotary_args(*rot, out, dt);
+        const size_t wsb = dvattn_paged_sdpa_rope_workspace_size(&a, &ra);
+        TORCH_CHECK(wsb > 0, "dvattn_paged_sdpa_rope: could not size the workspace (unsupported or invalid shape)");
+        at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
+        check_status(dvattn_paged_sdpa_rope(&a, &ra, ws.data_ptr(), wsb, cur_stream(out)), "dvattn_paged_sdpa_rope");
+        return;
     }
     int st = dvattn_paged_sdpa(&a, nullptr, 0, cur_stream(out));  // validation only when nothing to do
     if (st == DVATTN_ERR_WORKSPACE) {
@@ -153,22 +190,22 @@ void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, con
                  const at::Tensor& cosines, const at::Tensor& sines, const at::Tensor& fragment_lengths,
                  const at::Tensor& k_cache, const at::Tensor& v_cache, const at::Tensor& block_tables,
                  const at::Tensor& cu_seqlens_q, const at::Tensor& cu_seqlens_k, const c10::optional<at::Tensor>& lse,
-                 const c10::optional<at::Tensor>& out_f32) {
+                 const c10::optional<at::Tensor>& out_f32, const RotaryOpt* rot = nullptr) {
     const c10::cuda::CUDAGuard guard(out.device());
     const int dt = dtype_code(out);
-    TORCH_CHECK(queries.dim() == 3 && out.dim() == 3 && locations.dim() == 2 && cosines.dim() == 3 && sines.dim() == 3 &&
+    TORCH_CHECK(queries.dim() == 3 && out.dim() == 3 && locations.dim() == 2 && (rot || (cosines.dim() == 3 && sines.dim() == 3)) &&
                     k_cache.dim() == 4 && v_cache.dim() == 4 && block_tables.dim() == 2 && cu_seqlens_q.dim() == 1,
                 "dvattn_varlen_paged_sdpa: wrong tensor ranks");
     for (auto* pr : {&queries, &k_cache, &v_cache})
         TORCH_CHECK(pr->scalar_type() == out.scalar_type(), "dvattn_varlen_paged_sdpa: queries/k_cache/v_cache must have the output dtype");
-    TORCH_CHECK(cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat,
+    TORCH_CHECK(rot || (cosines.scalar_type() == at::kFloat && sines.scalar_type() == at::kFloat),
                 "dvattn_varlen_paged_sdpa: cosines/sines must be float32");
     check_i32(locations, "locations");
     check_i32(fragment_lengths, "fragment_lengths");
     check_i32(block_tables, "block_tables");
     check_i32(cu_seqlens_q, "cu_seqlens_q");
+    if (!rot) check_all(out, {Named{&cosines, "cosines"}, Named{&sines, "sines"}});
     check_all(out, {Named{&queries, "queries"}, Named{&locations, "locations"},
-                    Named{&cosines, "cosines"}, Named{&sines, "sines"},
                     Named{&fragment_lengths, "fragment_lengths"}, Named{&k_cache, "k_cache"},
                     Named{&v_cache, "v_cache"}, Named{&block_tables, "block_tables"},
                     Named{&cu_seqlens_q, "cu_seqlens_q"}, Named{&out, "output"}});
@@ -180,8 +217,10 @@ void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, con
     const int Ev = v_cache.size(3);
     TORCH_CHECK(W >= 0, "dvattn_varlen_paged_sdpa: cu_seqlens_q must have W+1 entries");
     TORCH_CHECK(locations.size(1) == T, "dvattn_varlen_paged_sdpa: locations must be [F, T]");
-    TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == T, "dvattn_varlen_paged_sdpa: cosines must be [F, T, R/2]");
-    TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_varlen_paged_sdpa: sines must match cosines");
+    if (!rot) {
+        TORCH_CHECK(cosines.size(0) == F && cosines.size(1) == T, "dvattn_varlen_paged_sdpa: cosines must be [F, T, R/2]");
+        TORCH_CHECK(sines.sizes() == cosines.sizes(), "dvattn_varlen_paged_sdpa: sines must match cosines");
+    }
     TORCH_CHECK(fragment_lengths.size(0) == F, "dvattn_varlen_paged_sdpa: fragment_lengths must be [F]");
     TORCH_CHECK(out.size(0) == T && out.size(1) == Hq && out.size(2) == Ev, "dvattn_varlen_paged_sdpa: output must be [T, Hq, Ev]");
     TORCH_CHECK(k_cache.size(3) == E, "dvattn_varlen_paged_sdpa: k_cache must be [NB, BS, Hkv, E]");
@@ -191,15 +230,15 @@ void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, con
     dvattn_varlen_args a{};
     a.dtype = dt;
     a.F = F; a.W = W; a.Hq = Hq; a.Hkv = k_cache.size(2); a.E = E; a.Ev = Ev; a.T = T;
-    a.R = cosines.size(2) * 2;
+    a.R = rot ? rot->R : cosines.size(2) * 2;
     a.block_size = k_cache.size(1);
     a.max_blocks_per_seq = block_tables.size(1);
     a.num_blocks = k_cache.size(0);
     a.scale = static_cast<float>(scale);
     a.out = out.data_ptr();
     a.queries = queries.const_data_ptr();
-    a.cosines = cosines.const_data_ptr<float>();
-    a.sines = sines.const_data_ptr<float>();
+    a.cosines = rot ? nullptr : cosines.const_data_ptr<float>();
+    a.sines = rot ? nullptr : sines.const_data_ptr<float>();
     a.locations = locations.const_data_ptr<int>();
     a.fragment_lengths = fragment_lengths.const_data_ptr<int>();
     a.k_cache = k_cache.const_data_ptr();
@@ -216,6 +255,15 @@ void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, con
         check_cuda_tensor(*out_f32, "out_f32", out);
         TORCH_CHECK(out_f32->scalar_type() == at::kFloat && out_f32->numel() == out.numel(), "dvattn: out_f32 must be f32 like output");
         a.out_f32 = out_f32->data_ptr<float>();
+    }
+    if (rot) {
+        const dvattn_rotary_args ra = rotary_args(*rot, out, dt);
+        const size_t wsb = dvattn_varlen_paged_sdpa_rope_workspace_size(&a, &ra);
+        TORCH_CHECK(wsb > 0, "dvattn_varlen_paged_sdpa_rope: could not size the workspace (unsupported or invalid shape)");
+        at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
+        check_status(dvattn_varlen_paged_sdpa_rope(&a, &ra, ws.data_ptr(), wsb, cur_stream(out)),
+                     "dvattn_varlen_paged_sdpa_rope");
+        return;
     }
     int st = dvattn_varlen_paged_sdpa(&a, nullptr, 0, cur_stream(out));
     if (st == DVATTN_ERR_WORKSPACE) {
@@ -244,6 +292,31 @@ void dvattn_varlen_paged_sdpa_ex_op(at::Tensor& out, const c10::optional<at::Ten
                                     const at::Tensor& cu_seqlens_k) {
     varlen_impl(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
                 cu_seqlens_q, cu_seqlens_k, lse, out_f32);
+}
+
+// The same two ops with the rotation tables built on the device from the locations
+// (the model's rotary embedding: theta, scaling, optional inv_freq; cos/sin rounded
+// through the output dtype as the model returns them).
+void dvattn_paged_sdpa_rope_op(at::Tensor& out, double scale, const at::Tensor& locations, const at::Tensor& queries,
+                               const at::Tensor& fragment_lengths, const at::Tensor& k_cache, const at::Tensor& v_cache,
+                               const at::Tensor& block_tables, int64_t rotary_dim, double rope_base,
+                               double attention_scaling, const c10::optional<at::Tensor>& inv_freq) {
+    const RotaryOpt rot{(int)rotary_dim, rope_base, attention_scaling, &inv_freq};
+    const at::Tensor none;
+    paged_impl(out, scale, locations, queries, none, none, fragment_lengths, k_cache, v_cache, block_tables,
+               c10::nullopt, c10::nullopt, &rot);
+}
+
+void dvattn_varlen_paged_sdpa_rope_op(at::Tensor& out, double scale, const at::Tensor& locations,
+                                      const at::Tensor& queries, const at::Tensor& fragment_lengths,
+                                      const at::Tensor& k_cache, const at::Tensor& v_cache,
+                                      const at::Tensor& block_tables, const at::Tensor& cu_seqlens_q,
+                                      const at::Tensor& cu_seqlens_k, int64_t rotary_dim, double rope_base,
+                                      double attention_scaling, const c10::optional<at::Tensor>& inv_freq) {
+    const RotaryOpt rot{(int)rotary_dim, rope_base, attention_scaling, &inv_freq};
+    const at::Tensor none;
+    varlen_impl(out, scale, locations, queries, none, none, fragment_lengths, k_cache, v_cache, block_tables,
+                cu_seqlens_q, cu_seqlens_k, c10::nullopt, c10::nullopt, &rot);
 }
 
 // ---------------------------------------------------------------------------------
@@ -520,6 +593,13 @@ TORCH_LIBRARY(libdvatt, m) {
           "Tensor locations, Tensor queries, Tensor cosines, Tensor sines, Tensor fragment_lengths, Tensor k_cache, "
           "Tensor v_cache, Tensor block_tables, Tensor cu_seqlens_q, Tensor cu_seqlens_k) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
     m.def("dvattn_lse_merge(Tensor(a!) output, Tensor(b!)? lse_out, Tensor part_out, Tensor part_lse) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_paged_sdpa_rope(Tensor(a!) output, float scale, Tensor locations, Tensor queries, "
+          "Tensor fragment_lengths, Tensor k_cache, Tensor v_cache, Tensor block_tables, int rotary_dim, "
+          "float rope_base, float attention_scaling, Tensor? inv_freq) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
+    m.def("dvattn_varlen_paged_sdpa_rope(Tensor(a!) output, float scale, Tensor locations, Tensor queries, "
+          "Tensor fragment_lengths, Tensor k_cache, Tensor v_cache, Tensor block_tables, Tensor cu_seqlens_q, "
+          "Tensor cu_seqlens_k, int rotary_dim, float rope_base, float attention_scaling, Tensor? inv_freq) -> ()",
+          tags, torch::_RegisterOrVerify::REGISTER);
     m.def("dvattn_build_views(Tensor(a!) locations, Tensor(b!) cosines, Tensor(c!) sines, Tensor seg_lengths, "
           "Tensor seg_order, Tensor? inv_freq, float rope_base, float attention_scaling, int round_dtype) -> ()", tags, torch::_RegisterOrVerify::REGISTER);
     m.def("dvattn_paged_append(Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor keys, Tensor values, Tensor cosines, "
@@ -538,4 +618,6 @@ TORCH_LIBRARY_IMPL(libdvatt, CUDA, m) {
     m.impl("dvattn_lse_merge", dvattn_lse_merge_op);
     m.impl("dvattn_paged_append", dvattn_paged_append_op);
     m.impl("dvattn_build_views", dvattn_build_views_op);
+    m.impl("dvattn_paged_sdpa_rope", dvattn_paged_sdpa_rope_op);
+    m.impl("dvattn_varlen_paged_sdpa_rope", dvattn_varlen_paged_sdpa_rope_op);
 }

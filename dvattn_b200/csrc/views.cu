@@ -14,7 +14,6 @@
 
 namespace dvb {
 
-template <class R> __device__ __forceinline__ float round_through(float x) { return Elem<R>::to_f(Elem<R>::from_f(x)); }
 
 __device__ __forceinline__ int view_location(const dvattn_views_args& a, long long row) {
     const int i = (int)(row % a.n);
@@ -27,22 +26,8 @@ __device__ __forceinline__ int view_location(const dvattn_views_args& a, long lo
     return (int)(suffix - a.n + i);
 }
 
-// cos/sin of rotary pair j at position pos: inv_freq_j = 1 / base^(2j / R) in f32,
-// freq = inv_freq_j * pos (one rounding), times attention_scaling, rounded through the
-// model dtype.
 __device__ __forceinline__ void view_cs(const dvattn_views_args& a, int j, float pos, float& c, float& s) {
-    const float inv = a.inv_freq ? __ldg(a.inv_freq + j) : 1.0f / powf(a.rope_base, (float)(2 * j) / (float)a.R);
-    const float ang = __fmul_rn(inv, pos);
-    sincosf(ang, &s, &c);  // one argument reduction for both
-    c *= a.attention_scaling;
-    s *= a.attention_scaling;
-    if (a.round_dtype == DVATTN_BFLOAT16) {
-        c = round_through<__nv_bfloat16>(c);
-        s = round_through<__nv_bfloat16>(s);
-    } else if (a.round_dtype == DVATTN_FLOAT16) {
-        c = round_through<__half>(c);
-        s = round_through<__half>(s);
-    }
+    rotary_cos_sin(a.inv_freq, a.rope_base, a.R, j, pos, a.attention_scaling, a.round_dtype, c, s);
 }
 
 // General form: a thread per (segment, worker, token) row.

@@ -163,6 +163,17 @@ typedef struct dvattn_views_args {
     float* sines;                 /* out [F,W,n,R] f32                                    */
 } dvattn_views_args;
 
+/*
+ * The model's rotary embedding, for the attention entry points that compute the query
+ * rotation tables on the device from the locations instead of taking cosines/sines.
+ */
+typedef struct dvattn_rotary_args {
+    float rope_base;              /* theta                                                */
+    float attention_scaling;      /* factor on cos/sin (1 for the default rotary)         */
+    int round_dtype;              /* DVATTN_*: cos/sin rounded through the model dtype    */
+    const float* inv_freq;        /* [R/2] f32 or null (1 / rope_base^(2j/R) on device)  */
+} dvattn_rotary_args;
+
 /* ABI version of this header (bumped on any layout change of the structs above). */
 int dvattn_abi_version(void);
 
@@ -267,6 +278,21 @@ int dvattn_paged_append(const dvattn_append_args* args, dvattn_stream_t stream);
  * rotary embedding of them).  Writes the locations, cosines and sines the attention ops take.
  */
 int dvattn_build_views(const dvattn_views_args* args, dvattn_stream_t stream);
+
+/*
+ * dvattn_paged_sdpa / dvattn_varlen_paged_sdpa with the query rotation tables computed on
+ * the device: the rotation of turn f for query (w, s) (token t) is the model's rotary
+ * embedding at its location loc[f, w, s] (loc[f, t]), as DVAttnCache.update builds the
+ * cos/sin it passes (python/dvattn/attention.py:161-191).  args->cosines / sines are
+ * ignored; args->R is the rotary dim.  The tables live in the workspace (one small
+ * kernel before the attention).
+ */
+size_t dvattn_paged_sdpa_rope_workspace_size(const dvattn_paged_args* args, const dvattn_rotary_args* rotary);
+int dvattn_paged_sdpa_rope(const dvattn_paged_args* args, const dvattn_rotary_args* rotary, void* workspace,
+                           size_t workspace_bytes, dvattn_stream_t stream);
+size_t dvattn_varlen_paged_sdpa_rope_workspace_size(const dvattn_varlen_args* args, const dvattn_rotary_args* rotary);
+int dvattn_varlen_paged_sdpa_rope(const dvattn_varlen_args* args, const dvattn_rotary_args* rotary, void* workspace,
+                                  size_t workspace_bytes, dvattn_stream_t stream);
 
 /*
  * Standalone query rotation, schema `dvattn_rope` (src/binding.cu:41-77, src/rope.cuh:2-65):

@@ -360,9 +360,18 @@ def build_views(seg_lengths, seg_order, n, R, rope_base, attention_scaling=1.0, 
     if R == 0:
         z = torch.zeros((F, W, n, 0))
         return loc, z, z.clone()
+    cos, sin = rotary_tables(loc, R, rope_base, attention_scaling, dtype)
+    return loc, cos, sin
+
+
+def rotary_tables(loc, R, rope_base, attention_scaling=1.0, dtype=torch.float32):
+    """The model's default rotary embedding at positions `loc` (any shape): cos/sin
+    [..., R] f32 with equal halves, computed as HF's rotary module does (inv_freq =
+    1 / base^(arange(0, R, 2) / R) in f32, freqs = pos * inv_freq, cat(freqs, freqs),
+    times attention_scaling, in the model dtype, widened to f32)."""
     inv_freq = 1.0 / (rope_base ** (torch.arange(0, R, 2, dtype=torch.int64).float() / R))
-    freqs = loc.float()[..., None] * inv_freq
+    freqs = torch.as_tensor(loc).float()[..., None] * inv_freq
     emb = torch.cat((freqs, freqs), dim=-1)
     cos = (emb.cos() * attention_scaling).to(dtype).to(torch.float32)
     sin = (emb.sin() * attention_scaling).to(dtype).to(torch.float32)
-    return loc, cos, sin
+    return cos, sin
