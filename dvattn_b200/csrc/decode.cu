@@ -2007,6 +2007,68 @@ size_t decode_workspace_size(const dvattn_paged_args* a) {
     return decode_layout(a->W * a->S, a->E, n_launch, false, kc.row ? a->Hkv : 1).total;
 }
 
+// Programmatic dependent launch lets a call's first kernel start while the kernel before it
+// in the stream still runs, and that kernel reads its inputs (block tables, locations,
+// queries, pages) before its griddepcontrol.wait.  That is sound only while the kernel
+// before it does not write those inputs.  This library's own kernels let their dependents
+// launch early, so the launcher remembers, per (device, stream), the output ranges of its
+// last call there and launches the next call's first kernel as an ordinary, fully ordered
+// launch when one of its inputs overlaps them (a call whose queries are the previous call's
+// output).  Early-triggering kernels of other libraries are not visible here:
+// DVATTN_PDL=0 makes every call's first kernel an ordinary launch.
+struct Span {
+    uintptr_t lo, hi;
+};
+static Span span_of(const void* p, long long bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    return (p && bytes > 0) ? Span{a, a + (uintptr_t)bytes} : Span{0, 0};
+}
+struct LastOutputs {
+    int dev;
+    cudaStream_t stream;
+    Span out[3];
+};
+static std::mutex g_last_mu;
+static LastOutputs g_last[64];
+static int g_last_n = 0, g_last_next = 0;
+
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("DVATTN_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+static bool first_launch_may_overlap(int dev, cudaStream_t s, const Span* in, int nin) {
+    if (!pdl_enabled()) return false;
+    std::lock_guard<std::mutex> lk(g_last_mu);
+    for (int i = 0; i < g_last_n; ++i) {
+        if (g_last[i].dev != dev || g_last[i].stream != s) continue;
+        for (const Span& o : g_last[i].out)
+            for (int j = 0; j < nin; ++j)
+                if (o.lo < o.hi && in[j].lo < in[j].hi && in[j].lo < o.hi && o.lo < in[j].hi) return false;
+        return true;
+    }
+    return true;
+}
+
+static void remember_outputs(int dev, cudaStream_t s, const Span* out) {
+    std::lock_guard<std::mutex> lk(g_last_mu);
+    int slot = -1;
+    for (int i = 0; i < g_last_n; ++i)
+        if (g_last[i].dev == dev && g_last[i].stream == s) slot = i;
+    if (slot < 0) {
+        if (g_last_n < 64) {
+            slot = g_last_n++;
+        } else {
+            slot = g_last_next;
+            g_last_next = (g_last_next + 1) % 64;
+        }
+    }
+    g_last[slot] = LastOutputs{dev, s, {out[0], out[1], out[2]}};
+}
+
 // Runs prep -> split kernel -> merge for a filled PagedParams (pointers, sizes, R,
 // cs_stride, cu_q/nseq); fills the workspace-derived fields.
 static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes, cudaStream_t stream, int phase) {
@@ -2018,6 +2080,28 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     int n_launch = 0;
     int st = device_sms_and_occ(kc, n_launch);
     if (st != DVATTN_OK) return st;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return DVATTN_ERR_CUDA;
+    const int esz = dtype == DVATTN_FLOAT32 ? 4 : 2;
+    const long long rowsz = (long long)p.WS * p.Hq * p.E;  // elements of queries / out per turn
+    std::vector<Span> in_spans;
+    in_spans.reserve(10 + 2 * (size_t)p.nfrag);
+    in_spans.push_back(span_of(p.q, (p.nfrag ? p.F : 1) * rowsz * esz));
+    in_spans.push_back(span_of(p.loc, 4LL * p.F * p.WS));
+    in_spans.push_back(span_of(p.L, 4LL * p.F));
+    in_spans.push_back(span_of(p.cos, 4LL * p.F * p.WS * p.cs_stride));
+    in_spans.push_back(span_of(p.sin, 4LL * p.F * p.WS * p.cs_stride));
+    in_spans.push_back(span_of(p.bt, 4LL * (p.cu_q ? p.nseq : p.W) * p.maxb));
+    in_spans.push_back(span_of(p.cu_q, 4LL * (p.nseq + 1)));
+    in_spans.push_back(span_of(p.k, p.NB * p.BS * p.Hkv * p.E * esz));
+    in_spans.push_back(span_of(p.v, p.NB * p.BS * p.Hkv * p.E * esz));
+    for (int f = 0; f < p.nfrag; ++f) {
+        const long long fb = (long long)p.frag[f].rows * (p.frag[f].wmul ? p.W : 1) * p.Hkv * p.E * esz;
+        in_spans.push_back(span_of(p.frag[f].k, fb));
+        in_spans.push_back(span_of(p.frag[f].v, fb));
+    }
+    const Span out_spans[3] = {span_of(p.out, rowsz * esz), span_of(p.out_f32, rowsz * 4),
+                               span_of(p.lse_out, 4LL * p.WS * p.Hq)};
     p.hsplit = kc.row ? 1 : p.Hkv;
     p.bs_shift = (p.BS & (p.BS - 1)) == 0 ? __builtin_ctz((unsigned)p.BS) : -1;
     p.slot_heads = kc.row ? p.Hkv : 1;
@@ -2074,7 +2158,6 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     }
     {
         // a query rotation costs about as long as streaming ~96 KB of the cache
-        const int esz = dtype == DVATTN_FLOAT32 ? 4 : 2;
         const long long unit_bytes = (long long)(kc.row ? p.Hkv : 1) * 2 * p.E * esz;
         const long long ru = (96 * 1024) / unit_bytes;
         p.rot_units = (int)(ru < 8 ? 8 : ru);
@@ -2087,6 +2170,9 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.fused = (kc.row && !p.cu_q && (size_t)(p.WS + 1 + 32) * 8 <= kc.sched_smem &&
                (long long)p.WS + 1 <= 32LL * n_launch) ? 1 : 0;
 
+    // the first kernel this call launches may overlap the kernel before it only if that
+    // kernel cannot have written this call's inputs (see first_launch_may_overlap)
+    const bool overlap_ok = first_launch_may_overlap(dev, stream, in_spans.data(), (int)in_spans.size());
     if ((phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) && !p.fused) {
         // programmatic dependent of whatever precedes it (the previous call's merge): it
         // computes the schedule before waiting, and writes it after
@@ -2098,7 +2184,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = overlap_ok ? 1 : 0;
         void* pargs[] = {&p};
         if (cudaLaunchKernelExC(&cfg, (const void*)&decode_prep_kernel, pargs) != cudaSuccess) return DVATTN_ERR_CUDA;
     }
@@ -2112,7 +2198,9 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        // the fused row kernel reads its inputs before griddepcontrol.wait; the others wait
+        // first (for the schedule kernel)
+        cfg.numAttrs = (!p.fused || overlap_ok) ? 1 : 0;
         if (kc.tma) {
             alignas(64) CUtensorMap mk, mv;
             const int win = kc.row ? 16 * kc.cw / p.Hkv : 64;
@@ -2174,6 +2262,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         void* margs[] = {&p};
         if (cudaLaunchKernelExC(&cfg, mk, margs) != cudaSuccess) return DVATTN_ERR_CUDA;
     }
+    if (phase != DVATTN_PHASE_SCHEDULE) remember_outputs(dev, stream, out_spans);
     return cudaGetLastError() == cudaSuccess ? DVATTN_OK : DVATTN_ERR_CUDA;
 }
 

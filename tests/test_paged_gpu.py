@@ -169,6 +169,34 @@ def test_deterministic_and_workspace_reuse():
     assert torch.equal(out1, out2)
 
 
+def test_chained_call_reads_previous_output():
+    """The second call's queries are the first call's output, with no other kernel between
+    them: the second call must see the merged output, not what the buffer held before
+    (the first kernel of a call may start early only when the previous call's outputs are
+    none of its inputs)."""
+    c = wl.config2(W=32).to(DEV)
+    out1 = torch.full_like(c.new_out(), float("nan"))
+    out2 = c.new_out()
+    args1 = list(c.op_args(out1))
+    args2 = list(c.op_args(out2))
+    args2[3] = out1  # queries of the second call
+    call1 = capi.PagedCall(*args1)
+    call2 = capi.PagedCall(*args2)
+    for _ in range(5):
+        out1.fill_(float("nan"))
+        call1()
+        call2()
+        torch.cuda.synchronize()
+        ref = out1.clone()
+        args3 = list(args2)
+        args3[0] = torch.empty_like(out2)
+        args3[3] = ref
+        capi.PagedCall(*args3)()
+        torch.cuda.synchronize()
+        assert not torch.isnan(out2).any()
+        assert torch.equal(out2, args3[0])
+
+
 def test_torch_op_on_side_stream_and_second_device_index():
     import dvattn_b200
     c = wl.make_paged([[300, 45], [17, 900]], Hq=32, Hkv=2, E=128, R=32, BS=16, dtype=torch.bfloat16, seed=1).to(DEV)
