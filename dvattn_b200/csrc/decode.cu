@@ -158,14 +158,14 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
 // the update is in place with no register staging.  The caller follows with a barrier.
 template <class T, int E>
 __device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, int f, int nh, uint8_t* sQ, int tid,
-                                                 int nth, int bar_id) {
+                                                 int nth, float* sCS, int bar_id) {
     constexpr int CH = E / 8;
     const int w = ws / p.S, s = ws - w * p.S;
     const float* cr = p.cos + ((size_t)f * p.WS + ws) * p.cs_stride;
     const float* sr = p.sin + ((size_t)f * p.WS + ws) * p.cs_stride;
     const int R = p.R, hp = R >> 1;
     if (!((hp & 7) == 0 && ((reinterpret_cast<uintptr_t>(cr) | reinterpret_cast<uintptr_t>(sr)) & 15) == 0)) {
-        rotate_q_rows<T, E, 1>(p, ws, f, 0, nh, sQ, tid, nth, nullptr, bar_id);  // general path (scalar)
+        rotate_q_rows<T, E, 1>(p, ws, f, 0, nh, sQ, tid, nth, sCS, bar_id);  // general path (scalar)
         return;
     }
     auto slot = [&](int row, int ch) -> uint8_t* {
@@ -178,24 +178,16 @@ __device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, i
                      (((size_t)w * p.Hq + (row >> 4) * p.gqa + (g < p.gqa ? g : 0)) * p.S + s) * E + ch * 8;
         cp_async16_zfill(smem_u32(slot(row, ch)), q, g < p.gqa ? 16 : 0);
     }
-    cp_async_commit();
-    // the cos/sin rows are read from global memory (the producer prefetched them into L2);
-    // pull their lines into L1 while the q copies are in flight
-    for (int k = tid; k < 2 * ((hp + 31) >> 5); k += nth) {
-        const int half = k / ((hp + 31) >> 5), line = k - half * ((hp + 31) >> 5);
-        asm volatile("prefetch.global.L1 [%0];" ::"l"((half ? sr : cr) + line * 32));
+    for (int k = tid; k < 2 * (hp >> 2); k += nth) {
+        const int half = k / (hp >> 2), jj = k - half * (hp >> 2);
+        cp_async16_zfill(smem_u32(sCS + half * hp + jj * 4), (half ? sr : cr) + jj * 4, 16);
     }
-    const int npair = hp >> 3;
+    cp_async_commit();
     cp_async_wait<0>();
     named_bar_sync(bar_id, nth);
+    const int npair = hp >> 3;
     for (int t = tid; t < nh * 16 * npair; t += nth) {
         const int row = t / npair, j = t - row * npair;
-        const float4 c_lo = __ldg(reinterpret_cast<const float4*>(cr + j * 8));
-        const float4 c_hi = __ldg(reinterpret_cast<const float4*>(cr + j * 8) + 1);
-        const float4 s_lo = __ldg(reinterpret_cast<const float4*>(sr + j * 8));
-        const float4 s_hi = __ldg(reinterpret_cast<const float4*>(sr + j * 8) + 1);
-        const float cc[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
-        const float ss[8] = {s_lo.x, s_lo.y, s_lo.z, s_lo.w, s_hi.x, s_hi.y, s_hi.z, s_hi.w};
         uint4* xa = reinterpret_cast<uint4*>(slot(row, j));
         uint4* ya = reinterpret_cast<uint4*>(slot(row, j + npair));
         uint4 xv = *xa, yv = *ya;
@@ -204,8 +196,8 @@ __device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, i
         uint32_t lo[4], hi[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float c0 = cc[2 * u], c1 = cc[2 * u + 1];
-            const float s0 = ss[2 * u], s1 = ss[2 * u + 1];
+            const float c0 = sCS[j * 8 + 2 * u], c1 = sCS[j * 8 + 2 * u + 1];
+            const float s0 = sCS[hp + j * 8 + 2 * u], s1 = sCS[hp + j * 8 + 2 * u + 1];
             const float x0 = Elem<T>::to_f(x[2 * u]), x1 = Elem<T>::to_f(x[2 * u + 1]);
             const float y0 = Elem<T>::to_f(y[2 * u]), y1 = Elem<T>::to_f(y[2 * u + 1]);
             lo[u] = Elem<T>::pack2(x0 * c0 - y0 * s0, x1 * c1 - y1 * s1);
@@ -953,17 +945,13 @@ struct RowCfg {
     // With q fragments held in registers (E <= 128) the rotation buffer is only used at a
     // turn change and the merge buffer only at a row's end, so the two share memory.
     static constexpr size_t OFF_O = QREG ? OFF_Q : OFF_Q + QBYTES;
-    // Stage descriptors, barriers and the abort flag come right after the q / merge
-    // buffers, and the cross-warp merge statistics (used only when several warps serve one
-    // KV head, Hkv < CW) last: a call with Hkv == CW is launched with SMEM_ONE_WARP_PER_HEAD
-    // bytes, which leaves room on the SM for a merge block beside two attention CTAs.
-    static constexpr size_t OFF_DESC = QREG ? OFF_Q + (QBYTES > OBYTES ? QBYTES : OBYTES) : OFF_O + OBYTES;
+    static constexpr size_t OFF_ML = QREG ? OFF_Q + (QBYTES > OBYTES ? QBYTES : OBYTES) : OFF_O + OBYTES;
+    static constexpr size_t OFF_LSE = OFF_ML + (CW * 16 * 2 > E ? CW * 16 * 2 : E) * 4;
+    static constexpr size_t OFF_DESC = OFF_LSE + 2 * 16 * 4;
     static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
     static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
-    static constexpr size_t SMEM_ONE_WARP_PER_HEAD = OFF_FLAG + 16;
-    static constexpr size_t OFF_ML = SMEM_ONE_WARP_PER_HEAD;
-    static constexpr size_t OFF_LSE = OFF_ML + CW * 16 * 2 * 4;
-    static constexpr size_t SMEM = OFF_LSE + 2 * 16 * 4;
+    static constexpr size_t OFF_CS = OFF_ML;  // cos/sin staging of a rotation aliases the merge stats
+    static constexpr size_t SMEM = OFF_FLAG + 16;
 };
 
 // Tensor maps of up to kParamFrags contiguous fragments, passed by value to the row kernel
@@ -1207,7 +1195,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         it0.align = TOKB;
         TileDesc d0;
         if (it0.next(p, d0)) {
-            rotate_q_inplace<T, E>(p, d0.ws, d0.f, Hkv, sQ, tid, CW * 32, 2);
+            rotate_q_inplace<T, E>(p, d0.ws, d0.f, Hkv, sQ, tid, CW * 32,
+                                                                           reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -1248,7 +1237,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             if (tid == 0) DVB_TADD(6, tr0);
 #endif
             named_bar_sync(2, CW * 32);
-            rotate_q_inplace<T, E>(p, d.ws, d.f, Hkv, sQ, tid, CW * 32, 2);
+            rotate_q_inplace<T, E>(p, d.ws, d.f, Hkv, sQ, tid, CW * 32,
+                                                                           reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -1803,139 +1793,6 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
 #endif
 }
 
-// Largest c < n with cstart[c] <= x (x >= cstart[0]) for two values at once, searched by
-// one warp: each round probes 32 evenly spaced boundaries per value with one load per lane,
-// so the search costs about log32(n) memory latencies instead of log2(n).
-__device__ __forceinline__ void warp_cta_of2(const long long* cst, long long x0, long long x1, int n, int lane,
-                                             int& c0, int& c1) {
-    int lo0 = 0, len0 = n, lo1 = 0, len1 = n;
-    while (len0 > 1 || len1 > 1) {
-        const int st0 = (len0 + 31) >> 5, st1 = (len1 + 31) >> 5;
-        const bool in0 = len0 > 1 && lane * st0 < len0, in1 = len1 > 1 && lane * st1 < len1;
-        const long long v0 = in0 ? cst[lo0 + lane * st0] : 0, v1 = in1 ? cst[lo1 + lane * st1] : 0;
-        const unsigned m0 = __ballot_sync(~0u, in0 && v0 <= x0), m1 = __ballot_sync(~0u, in1 && v1 <= x1);
-        if (len0 > 1) {
-            const int L = m0 ? 31 - __clz(m0) : 0;
-            lo0 += L * st0;
-            len0 = min(st0, len0 - L * st0);
-        }
-        if (len1 > 1) {
-            const int L = m1 ? 31 - __clz(m1) : 0;
-            lo1 += L * st1;
-            len1 = min(st1, len1 - L * st1);
-        }
-    }
-    c0 = lo0;
-    c1 = lo1;
-}
-
-// Merge of split rows for the row kernel, shaped to fit on an SM beside two attention
-// CTAs: one warp per block, no shared memory, at most 168 registers.  Its blocks become
-// resident while the attention grid still runs, so the next call's attention kernel (a
-// programmatic dependent of this one) launches at once instead of waiting for attention
-// CTAs to retire.  Item i = query rows [8 (i % 2), +8) of (row, KV head) segment i / 2;
-// block b takes items b, b + gridDim.x, ...; lane l owns columns [4l, 4l + 4) (E = 128).
-// Same log-sum-exp combination as decode_merge_kernel (paged_kernel_v21.cuh:347-363).
-template <class T>
-__global__ void __launch_bounds__(32, 12) decode_merge_warp_kernel(PagedParams p) {
-    constexpr int E = 128, RW = 8;
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int lane = threadIdx.x;
-    const int n = p.sched->n_eff;
-    const int nitem = 2 * p.WS * p.Hkv;
-    for (int it = blockIdx.x; it < nitem; it += gridDim.x) {
-        const int g_seg = it >> 1, r0 = (it & 1) * RW;
-        const int nr = min(RW, p.gqa - r0);  // rows of this item that exist
-        if (nr <= 0) continue;
-        const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
-        const long long P0 = p.P[ws], V = p.P[ws + 1] - P0;
-        const int w = ws / p.S, s = ws - w * p.S;
-        const size_t orow0 = ((size_t)w * p.Hq + hkv * p.gqa + r0) * p.S + s;  // row r: orow0 + r * S
-        if (V == 0) {
-            for (int r = 0; r < nr; ++r) {
-                const size_t orow = orow0 + (size_t)r * p.S;
-                store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * lane, 0.f, 0.f, 0.f, 0.f);
-                if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (p.lse_out && lane == 0) p.lse_out[orow] = neg_inf();
-            }
-            continue;
-        }
-        const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
-        int ca, cb;
-        warp_cta_of2(p.cstart, b, b + V - 1, n, lane, ca, cb);
-        if (ca == cb) continue;  // one piece: the attention kernel wrote the row
-        const int hh = p.slot_heads > 1 ? hkv : 0;
-        float4 acc[RW];
-        float M[RW], den[RW];
-#pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-            M[r] = neg_inf();
-            den[r] = 0.f;
-        }
-        const long long cst_a = p.cstart[ca];
-        for (int c0 = ca; c0 <= cb; c0 += 32) {
-            // lane j: piece of CTA c0 + j (its slot, or -1 for none / an empty CTA range)
-            const int cc = c0 + lane;
-            int pb = -1;
-            if (cc <= cb) {
-                const long long a0 = p.cstart[cc], a1 = p.cstart[cc + 1];
-                const int slot = (cc == ca && cst_a < b) ? 2 * ca + 1 : 2 * cc;
-                pb = a0 == a1 ? -1 : (slot * p.slot_heads + hh) * 16 + r0;
-            }
-            float wj[RW];
-#pragma unroll
-            for (int r = 0; r < RW; ++r) wj[r] = (pb >= 0 && r < nr) ? p.part_lse[pb + r] : neg_inf();
-#pragma unroll
-            for (int r = 0; r < RW; ++r) {
-                float mg = wj[r];
-#pragma unroll
-                for (int o = 16; o; o >>= 1) mg = fmaxf(mg, __shfl_xor_sync(~0u, mg, o));
-                const float mn = fmaxf(M[r], mg);
-                if (mn == neg_inf()) {
-                    wj[r] = 0.f;
-                    continue;
-                }
-                const float sc = fast_exp2(M[r] - mn);  // 0 while M is -inf
-                wj[r] = fast_exp2(wj[r] - mn);           // 0 for missing pieces
-                float sum = wj[r];
-#pragma unroll
-                for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(~0u, sum, o);
-                den[r] = den[r] * sc + sum;
-                acc[r].x *= sc; acc[r].y *= sc; acc[r].z *= sc; acc[r].w *= sc;
-                M[r] = mn;
-            }
-            const int cnt = min(32, cb - c0 + 1);
-#pragma unroll 2
-            for (int j = 0; j < cnt; ++j) {
-                const int pj = __shfl_sync(~0u, pb, j);
-                if (pj < 0) continue;
-                float4 v[RW];
-#pragma unroll
-                for (int r = 0; r < RW; ++r)
-                    v[r] = r < nr ? reinterpret_cast<const float4*>(p.part_o + (size_t)(pj + r) * E)[lane]
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int r = 0; r < RW; ++r) {
-                    const float g = __shfl_sync(~0u, wj[r], j);
-                    acc[r].x += g * v[r].x; acc[r].y += g * v[r].y; acc[r].z += g * v[r].z; acc[r].w += g * v[r].w;
-                }
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            if (r >= nr) break;
-            const size_t orow = orow0 + (size_t)r * p.S;
-            const float inv = den[r] > 0.f ? 1.f / den[r] : 0.f;
-            const float4 o = make_float4(acc[r].x * inv, acc[r].y * inv, acc[r].z * inv, acc[r].w * inv);
-            store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * lane, o.x, o.y, o.z, o.w);
-            if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[lane] = o;
-            if (p.lse_out && lane == 0) p.lse_out[orow] = den[r] > 0.f ? (M[r] + __log2f(den[r])) * kLn2 : neg_inf();
-        }
-    }
-}
-
 // ==================================================================================
 // host side
 // ==================================================================================
@@ -1950,7 +1807,6 @@ struct KernelChoice {
     bool row = false;  // all KV heads per CTA (hsplit = 1)
     int cw = 4;
     size_t sched_smem = 0;  // shared bytes the row kernel lends to its in-kernel schedule
-    size_t smem_one = 0;    // row kernel: shared bytes of a launch with one warp per KV head
 };
 
 template <class T, int E, int CW, int STAGES>
@@ -1960,7 +1816,6 @@ KernelChoice row_choice() {
     k.row = true;
     k.cw = CW;
     k.sched_smem = 2 * C::OFF_V;
-    k.smem_one = C::SMEM_ONE_WARP_PER_HEAD;
     return k;
 }
 
@@ -2105,47 +1960,6 @@ static int device_sms_and_occ(const KernelChoice& kc, int& n_launch) {
     std::lock_guard<std::mutex> lk(mu);
     if (ncache < 256) cache[ncache++] = {dev, kc.fn, n_launch};
     return DVATTN_OK;
-}
-
-// Whether one decode_merge_warp_kernel block fits on an SM beside the row kernel's CTAs
-// launched with `smem` bytes each (shared memory incl. the per-block reservation, and
-// registers per warp), computed once per (device, kernel).
-static bool merge_warp_fits(const KernelChoice& kc, size_t smem, int n_launch, const void* merge_fn) {
-    struct Entry {
-        int dev;
-        const void* fn;
-        size_t smem;
-        bool fits;
-    };
-    static Entry cache[64];
-    static int ncache = 0;
-    static std::mutex mu;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return false;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        for (int i = 0; i < ncache; ++i)
-            if (cache[i].dev == dev && cache[i].fn == kc.fn && cache[i].smem == smem) return cache[i].fits;
-    }
-    int sms = 0, smem_sm = 0, resv = 0, regs_sm = 0;
-    cudaFuncAttributes fa{}, fm{};
-    bool fits = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
-                cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess &&
-                cudaDeviceGetAttribute(&resv, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess &&
-                cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) == cudaSuccess &&
-                cudaFuncGetAttributes(&fa, kc.fn) == cudaSuccess && cudaFuncGetAttributes(&fm, merge_fn) == cudaSuccess;
-    if (fits && sms > 0) {
-        const long long occ = (n_launch + sms - 1) / sms;
-        auto warp_regs = [](int r) { return (long long)((r * 32 + 255) / 256) * 256; };
-        const long long sm_need = occ * ((long long)smem + fa.sharedSizeBytes + resv) + fm.sharedSizeBytes + resv;
-        const long long reg_need = occ * ((kc.nt + 31) / 32) * warp_regs(fa.numRegs) + warp_regs(fm.numRegs);
-        fits = sm_need <= smem_sm && reg_need <= regs_sm;
-    } else {
-        fits = false;
-    }
-    std::lock_guard<std::mutex> lk(mu);
-    if (ncache < 64) cache[ncache++] = {dev, kc.fn, smem, fits};
-    return fits;
 }
 
 struct DecodeLayout {
@@ -2359,16 +2173,6 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     // the first kernel this call launches may overlap the kernel before it only if that
     // kernel cannot have written this call's inputs (see first_launch_may_overlap)
     const bool overlap_ok = first_launch_may_overlap(dev, stream, in_spans.data(), (int)in_spans.size());
-    // row kernel with one warp per KV head: the smaller shared-memory launch, and the
-    // one-warp merge when its blocks fit beside the attention CTAs
-    const bool one_warp = kc.row && p.Hkv == kc.cw;
-    const size_t attn_smem = one_warp ? kc.smem_one : kc.smem;
-    const void* warp_merge = nullptr;
-    if (one_warp && p.E == 128 && dtype != DVATTN_FLOAT32) {
-        const void* fn = dtype == DVATTN_FLOAT16 ? (const void*)&decode_merge_warp_kernel<__half>
-                                                 : (const void*)&decode_merge_warp_kernel<__nv_bfloat16>;
-        if (merge_warp_fits(kc, attn_smem, n_launch, fn)) warp_merge = fn;
-    }
     if ((phase == DVATTN_PHASE_ALL || phase == DVATTN_PHASE_SCHEDULE) && !p.fused) {
         // programmatic dependent of whatever precedes it (the previous call's merge): it
         // computes the schedule before waiting, and writes it after
@@ -2388,7 +2192,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(n_launch);
         cfg.blockDim = dim3(kc.nt);
-        cfg.dynamicSmemBytes = attn_smem;
+        cfg.dynamicSmemBytes = kc.smem;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -2449,14 +2253,6 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         const long long nseg = (long long)p.WS * p.Hkv;
         cfg.gridDim = dim3((unsigned)(nseg < DVB_MERGE_CTAS ? nseg : DVB_MERGE_CTAS));
         cfg.blockDim = dim3(16 * p.E / 4);
-        if (warp_merge) {
-            // one block per SM at most, each beside the attention CTAs of its SM
-            int sms = 1;
-            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 1;
-            mk = warp_merge;
-            cfg.gridDim = dim3((unsigned)(2 * nseg < sms ? 2 * nseg : (long long)sms));
-            cfg.blockDim = dim3(32);
-        }
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
