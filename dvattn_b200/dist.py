@@ -81,9 +81,13 @@ def allgather_merge(out_f32: torch.Tensor, lse: torch.Tensor, out: torch.Tensor,
     every rank of `group` and merge them into `out` on every rank.  `merge` defaults to
     the CUDA merge kernel; it is injectable so the exchange logic can run on CPU ranks."""
     world = dist.get_world_size(group)
-    po = [torch.empty_like(out_f32) for _ in range(world)]
-    pl = [torch.empty_like(lse) for _ in range(world)]
-    dist.all_gather(po, out_f32.contiguous(), group=group)
-    dist.all_gather(pl, lse.contiguous(), group=group)
-    po, pl = torch.stack(po), torch.stack(pl)
+    # gathered straight into the [parts, ...] layout the merge reads (no per-rank list, no stack)
+    # (ranks concatenated along dim 0, which every backend accepts, then viewed as parts)
+    o, l = out_f32.contiguous().reshape(-1), lse.contiguous().reshape(-1)
+    po = torch.empty(world * o.numel(), dtype=o.dtype, device=o.device)
+    pl = torch.empty(world * l.numel(), dtype=l.dtype, device=l.device)
+    dist.all_gather_into_tensor(po, o, group=group)
+    dist.all_gather_into_tensor(pl, l, group=group)
+    po = po.view((world,) + tuple(out_f32.shape))
+    pl = pl.view((world,) + tuple(lse.shape))
     return (merge or _cuda_merge)(po, pl, out, lse_out)
