@@ -253,3 +253,39 @@ def test_error_flag_clear_after_calls():
     torch.cuda.synchronize()
     hdr = call.workspace[:16].cpu().view(torch.int32)
     assert int(hdr[3]) == 0  # {U (int64), n_eff, error}
+
+
+_PDL_CHILD = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from dvattn_b200 import capi
+from dvattn_b200 import workloads as wl
+c = wl.config2(W=8).to("cuda:0")
+out = c.new_out()
+call = capi.PagedCall(*c.op_args(out))
+for _ in range(3):
+    call()
+torch.cuda.synchronize()
+torch.save(out.cpu(), sys.argv[2])
+"""
+
+
+def test_pdl_switch_off_gives_identical_output(tmp_path):
+    """DVATTN_PDL=0 (every call's first kernel an ordinary launch) changes only launch
+    ordering: the output is bit-identical to the default launch."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    dst = str(tmp_path / "pdl_off.pt")
+    env = dict(os.environ, DVATTN_PDL="0")
+    r = subprocess.run([sys.executable, "-c", _PDL_CHILD, root, dst], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    c = wl.config2(W=8).to(DEV)
+    out = c.new_out()
+    call = capi.PagedCall(*c.op_args(out))
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), torch.load(dst))
