@@ -48,6 +48,7 @@ EXPORTS = [
     "dvattn_rope",
     "dvattn_varlen_rope",
     "dvattn_lse_merge",
+    "dvattn_lse_merge_packed",
     "dvattn_sdpa_workspace_size",
     "dvattn_sdpa",
     "dvattn_paged_append",
@@ -144,6 +145,8 @@ def lib() -> ctypes.CDLL:
         L.dvattn_varlen_rope.argtypes = [_i] * 6 + [_vp] * 5
         L.dvattn_lse_merge.restype = _i
         L.dvattn_lse_merge.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp, _vp]
+        L.dvattn_lse_merge_packed.restype = _i
+        L.dvattn_lse_merge_packed.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp]
         L.dvattn_paged_append.restype = _i
         L.dvattn_paged_append.argtypes = [ctypes.POINTER(AppendArgs), _vp]
         L.dvattn_paged_sdpa_rope_workspace_size.restype = ctypes.c_size_t
@@ -313,6 +316,21 @@ def lse_merge(part_out, part_lse, out, lse_out=None):
                                 out.data_ptr(), _ptr(lse_out), _stream(None))
     if st != DVATTN_OK:
         raise DvattnError(st, "dvattn_lse_merge")
+    return out
+
+
+def lse_merge_packed(packed, out, lse_out=None):
+    """dvattn_lse_merge_packed: packed f32 [parts, rows * (Ev + 1)] (each part's outputs, then
+    its LSEs) -> out [..., Ev]."""
+    Ev = out.size(-1)
+    rows = out.numel() // Ev
+    parts = packed.size(0)
+    if packed.dtype != torch.float32 or not packed.is_contiguous() or packed.numel() != parts * rows * (Ev + 1):
+        raise ValueError("lse_merge_packed: packed must be contiguous f32 [parts, rows * (Ev + 1)]")
+    st = lib().dvattn_lse_merge_packed(_DTYPE.get(out.dtype, -1), parts, rows, Ev, packed.data_ptr(), out.data_ptr(),
+                                       _ptr(lse_out), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_lse_merge_packed")
     return out
 
 

@@ -90,4 +90,10 @@ int dvattn_lse_merge(int dtype, int num_parts, long long rows, int Ev, const flo
                                  reinterpret_cast<cudaStream_t>(stream));
 }
 
+int dvattn_lse_merge_packed(int dtype, int num_parts, long long rows, int Ev, const float* packed, void* out,
+                            float* lse_out, dvattn_stream_t stream) {
+    return dvb::lse_merge_packed_launch(dtype, num_parts, rows, Ev, packed, out, lse_out,
+                                        reinterpret_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -37,5 +37,7 @@ int varlen_rope_launch(int dtype, int F, int T, int H, int E, int R, void* out, 
                        const float* sin, cudaStream_t stream);
 int lse_merge_launch(int dtype, int num_parts, long long rows, int Ev, const float* part_out, const float* part_lse,
                      void* out, float* lse_out, cudaStream_t stream);
+int lse_merge_packed_launch(int dtype, int parts, long long rows, int Ev, const float* packed, void* out,
+                            float* lse_out, cudaStream_t stream);
 
 }  // namespace dvb

@@ -91,3 +91,36 @@ def allgather_merge(out_f32: torch.Tensor, lse: torch.Tensor, out: torch.Tensor,
     po = po.view((world,) + tuple(out_f32.shape))
     pl = pl.view((world,) + tuple(lse.shape))
     return (merge or _cuda_merge)(po, pl, out, lse_out)
+
+
+def packed_partials(out: torch.Tensor):
+    """One f32 buffer holding a rank's partial outputs (shape of `out`) followed by its
+    natural-log LSEs (shape out.shape[:-1]), so that allgather_merge_packed exchanges both
+    in a single collective.  Returns (packed, out_f32 view, lse view); pass the views as the
+    attention call's out_f32 / lse outputs."""
+    Ev = out.size(-1)
+    rows = out.numel() // Ev
+    packed = torch.empty(rows * (Ev + 1), dtype=torch.float32, device=out.device)
+    return packed, packed[: rows * Ev].view(out.shape), packed[rows * Ev:].view(out.shape[:-1])
+
+
+def allgather_merge_packed(packed: torch.Tensor, out: torch.Tensor, group=None, merge: Optional[Callable] = None,
+                           lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """allgather_merge with one all-gather: `packed` is this rank's buffer from
+    packed_partials.  The default merge reads the gathered parts in place
+    (dvattn_lse_merge_packed); an injected `merge` gets the same (part_out, part_lse, out,
+    lse_out) arguments as in allgather_merge."""
+    world = dist.get_world_size(group)
+    Ev = out.size(-1)
+    rows = out.numel() // Ev
+    if packed.numel() != rows * (Ev + 1) or packed.dtype != torch.float32:
+        raise ValueError("allgather_merge_packed: packed must be f32 with rows * (Ev + 1) elements")
+    g = torch.empty(world * packed.numel(), dtype=torch.float32, device=packed.device)
+    dist.all_gather_into_tensor(g, packed.contiguous().reshape(-1), group=group)
+    g = g.view(world, rows * (Ev + 1))
+    if merge is None:
+        from . import capi
+        return capi.lse_merge_packed(g, out, lse_out)
+    po = g[:, : rows * Ev].reshape((world,) + tuple(out.shape))
+    pl = g[:, rows * Ev:].reshape((world,) + tuple(out.shape[:-1]))
+    return merge(po, pl, out, lse_out)

@@ -321,6 +321,15 @@ int dvattn_varlen_rope(int dtype, int F, int T, int H, int E, int R, void* out,
 int dvattn_lse_merge(int dtype, int num_parts, long long rows, int Ev, const float* part_out,
                      const float* part_lse, void* out, float* lse_out, dvattn_stream_t stream);
 
+/*
+ * dvattn_lse_merge over packed parts, as one collective gathers them: part i starts at
+ * packed + i * rows * (Ev + 1) floats and holds its [rows][Ev] outputs followed by its
+ * [rows] LSEs.  Lets each rank of a KV-sharded call exchange outputs and LSEs in a single
+ * all-gather (no reference counterpart: the reference runs on one GPU).
+ */
+int dvattn_lse_merge_packed(int dtype, int num_parts, long long rows, int Ev, const float* packed,
+                            void* out, float* lse_out, dvattn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

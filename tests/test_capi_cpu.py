@@ -86,6 +86,9 @@ def test_rope_and_merge_validation_without_gpu():
     assert lib.dvattn_lse_merge(capi.DVATTN_FLOAT32, 2, 0, 128, None, None, None, None, None) == capi.DVATTN_OK
     assert lib.dvattn_lse_merge(capi.DVATTN_FLOAT32, 2, 4, 0, None, None, None, None, None) == \
         capi.DVATTN_ERR_INVALID_ARGUMENT
+    assert lib.dvattn_lse_merge_packed(capi.DVATTN_FLOAT32, 2, 0, 128, None, None, None, None) == capi.DVATTN_OK
+    assert lib.dvattn_lse_merge_packed(capi.DVATTN_FLOAT32, 2, 4, 128, None, None, None, None) == \
+        capi.DVATTN_ERR_INVALID_ARGUMENT
 
 
 # the schemas of the reference extension (src/binding.cu:410-420)

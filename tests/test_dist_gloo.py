@@ -81,6 +81,29 @@ def test_kv_chunk_sharding_and_merge_world2():
     assert all(v == "ok" for v in res.values()), res
 
 
+def _kv_shard_and_merge_packed(rank, world):
+    c = _long_context_case()
+    sh = ddist.kv_chunk_shard(c, rank, world)
+    o32, lse = O.paged_sdpa_f32(sh.scale, sh.locations, sh.queries, sh.cosines, sh.sines, sh.fragment_lengths,
+                                sh.k_cache, sh.v_cache, sh.block_tables)
+    packed, po, pl = ddist.packed_partials(o32)
+    po.copy_(o32)
+    pl.copy_(lse)
+    out = torch.empty_like(o32)
+    lse_out = torch.empty_like(lse)
+    ddist.allgather_merge_packed(packed, out, merge=_oracle_merge, lse_out=lse_out)
+    ref, rlse = O.paged_sdpa_f32(c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths,
+                                 c.k_cache, c.v_cache, c.block_tables)
+    torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(lse_out, rlse, rtol=1e-5, atol=1e-5)
+
+
+def test_kv_chunk_sharding_and_packed_merge_world2():
+    """One all-gather of the packed (outputs, LSEs) buffer per rank gives the unsharded result."""
+    res = _run(_kv_shard_and_merge_packed)
+    assert all(v == "ok" for v in res.values()), res
+
+
 def _batch_shard(rank, world):
     tl = wl.config2_lengths(2, 12)
     weights = [sum(t) for t in tl]

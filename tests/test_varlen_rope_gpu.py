@@ -127,6 +127,28 @@ def test_lse_merge_kernel(dtype):
     assert torch.all(out[7] == 0)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_lse_merge_packed_kernel(dtype):
+    """Packed parts (outputs then LSEs per part, as one all-gather lays them out) merge to
+    the same result as the separate-buffer entry point, bit for bit."""
+    torch.manual_seed(1)
+    P, rows, Ev = 3, 29, 128
+    po = torch.randn(P, rows, Ev)
+    pl = torch.randn(P, rows) * 3
+    pl[2, :4] = float("-inf")
+    pl[:, 9] = float("-inf")
+    packed = torch.cat([po.reshape(P, -1), pl], dim=1).contiguous().to(DEV)
+    out = torch.empty(rows, Ev, dtype=dtype, device=DEV)
+    lo = torch.empty(rows, device=DEV)
+    capi.lse_merge_packed(packed, out, lo)
+    out2 = torch.empty_like(out)
+    lo2 = torch.empty_like(lo)
+    capi.lse_merge(po.to(DEV), pl.to(DEV), out2, lo2)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2) and torch.equal(lo, lo2)
+    assert torch.all(out[9] == 0)
+
+
 def test_split_kv_across_parts_equals_whole():
     """A long sequence cut into page-aligned KV chunks, each run as its own paged call with
     LSE output, merges back to the unsplit result (the multi-GPU long-context path)."""
