@@ -45,6 +45,73 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
+def _wl():
+    """dvattn_b200/workloads.py loaded by file path: the seeded input generators (torch and
+    numpy only).  Importing it this way does not run the package's __init__, so the
+    reference arm never loads this repository's native libraries."""
+    import importlib.util
+    name = "dvattn_b200_workloads"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(name, os.path.join(ROOT, "dvattn_b200", "workloads.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
+WORKLOAD_DESC = {
+    "config1": "config1: fp32 W=1 Hq=16 Hkv=1 E=128 R=64 L=1024 BS=16",
+    "config2": "config2: bf16 batched paged decode W=32 Hq=64 Hkv=4 E=128 R=64 BS=16 2 turns",
+    "config3": "config3: fp16 long context W=4 Hq=128 Hkv=8 E=128 R=128 L=131072 BS=64",
+    "config5": "config5: fp16 serving mix W=256 Hq=32 Hkv=2 E=256 R=64 BS=64 1-4 turns",
+}
+
+
+def paged_config(name: str, nbytes: int, world: int, pool_bytes: int) -> dict:
+    """The `config` object of a paged-decode bench line (identical in both arms)."""
+    return {"workload": WORKLOAD_DESC[name], "bytes_per_step_per_gpu": nbytes,
+            "parallelism": f"batch-replica x{world}",
+            "l2": "inputs larger than L2: 3 rotating KV pools of %.0f MB each" % (pool_bytes / 1e6)}
+
+
+def timed_reps(step, steps: int, world: int, stream, min_reps: int = 25, min_s: float = 1.0):
+    """Time `steps` calls of step(i) between CUDA events on `stream`, repeated: at least
+    `min_reps` times and until about `min_s` seconds of timed work (the rep count is agreed
+    over the ranks).  Each rep is bracketed by a barrier and a device synchronise; its
+    duration is the max over ranks.  Returns the per-rep ms list and the total wall time."""
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k = 0
+
+    def rep():
+        nonlocal k
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(steps):
+            step(k)
+            k += 1
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    first = rep()
+    reps = int(max_over_ranks(float(max(min_reps, min(5000, int(min_s * 1e3 / max(first, 1e-3)) + 1))), world))
+    times = [first] + [rep() for _ in range(reps - 1)]
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor(times, dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times = t.tolist()
+    return times
+
+
+def spread(per_rep_ms, steps: int) -> dict:
+    v = sorted(x / steps for x in per_rep_ms)
+    q = lambda f: v[min(len(v) - 1, int(f * (len(v) - 1) + 0.5))]  # noqa: E731
+    return {"reps": len(v), "min": round(v[0], 5), "p10": round(q(0.1), 5), "median": round(q(0.5), 5),
+            "p90": round(q(0.9), 5), "max": round(v[-1], 5), "unit": "ms per step"}
+
+
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -258,7 +325,7 @@ def cpu_sample_gbs(case_fn, n_seq: int, reps: int = 3):
     """Time oracle.paged_via_sdpa_pt (dvattn_sdpa_pt + apply_rotary_pos_emb restated) on the
     first n_seq sequences of the workload; returns (GB/s, threads, description)."""
     from oracle import dvattn_oracle as O
-    from dvattn_b200 import workloads as wl
+    wl = _wl()
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
     c = case_fn(n_seq)
@@ -278,20 +345,15 @@ def cpu_sample_gbs(case_fn, n_seq: int, reps: int = 3):
 # workloads
 # ------------------------------------------------------------------------------------
 def workload_case(name: str, device: str, rank: int = 0, world: int = 1):
-    from dvattn_b200 import workloads as wl
-    if name == "config2":
-        return wl.config2(device=device), "config2: bf16 batched paged decode W=32 Hq=64 Hkv=4 E=128 R=64 BS=16 2 turns"
-    if name == "config1":
-        return wl.config1(device=device), "config1: fp32 W=1 Hq=16 Hkv=1 E=128 R=64 L=1024 BS=16"
-    if name == "config3":
-        return wl.config3(device=device), "config3: fp16 long context W=4 Hq=128 Hkv=8 E=128 R=128 L=131072 BS=64"
-    if name == "config5":
-        return wl.config5(device=device), "config5: fp16 serving mix W=256 Hq=32 Hkv=2 E=256 R=64 BS=64 1-4 turns"
-    raise SystemExit(f"unknown workload {name}")
+    wl = _wl()
+    fn = {"config1": wl.config1, "config2": wl.config2, "config3": wl.config3, "config5": wl.config5}.get(name)
+    if fn is None:
+        raise SystemExit(f"unknown workload {name}")
+    return fn(device=device), WORKLOAD_DESC[name]
 
 
 def cpu_case_fn(name: str):
-    from dvattn_b200 import workloads as wl
+    wl = _wl()
     if name == "config2":
         return lambda n: wl.make_paged(wl.config2_lengths(2, 32)[:n], Hq=64, Hkv=4, E=128, R=64, BS=16,
                                        dtype=torch.bfloat16, seed=2)
@@ -315,33 +377,59 @@ CPU_SAMPLE = {"config2": (4, "first 4 of the 32 sequences of config 2"),
 
 def run_reference(args, world, rank):
     """--impl reference: the reference's own CPU implementation of the path (its
-    pure-PyTorch dvattn_sdpa_pt, restated in oracle/) on the host cores."""
+    pure-PyTorch dvattn_sdpa_pt + apply_rotary_pos_emb, restated in oracle/) on the host
+    cores.  Nothing of this repository's native code is loaded: the inputs come from
+    workloads.py loaded by path.  Config 2 (the default) and config 1 run whole; the larger
+    configs run on a bounded sample (named in the line, same_config false)."""
     if rank != 0:
         return
     name = "config3" if args.workload == "long3" else args.workload
-    n, desc = CPU_SAMPLE[name]
-    fn = cpu_case_fn(name)
-    from dvattn_b200 import workloads as wl
+    if name not in WORKLOAD_DESC:
+        print(json.dumps({"impl": "reference", "unavailable": f"no reference arm for workload {args.workload}"}))
+        return
+    wl = _wl()
     from oracle import dvattn_oracle as O
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    c = fn(n)
-    a = (c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
-         c.block_tables)
+    if name in ("config1", "config2"):
+        c = wl.config1() if name == "config1" else wl.config2()
+        same = True
+        W = c.queries.size(0)
+        # one reference call per sequence, each sequence's fragments cut at its own
+        # visible length (a caller of the eager path holds per-sequence fragments)
+        subs = [(c.scale, c.locations[:, w:w + 1], c.queries[w:w + 1], c.cosines[:, w:w + 1], c.sines[:, w:w + 1],
+                 c.fragment_lengths, c.k_cache, c.v_cache, c.block_tables[w:w + 1]) for w in range(W)]
+        desc = f"the whole workload ({W} sequences, one reference call per sequence)"
+    else:
+        n, desc = CPU_SAMPLE[name]
+        c = cpu_case_fn(name)(n)
+        same = False
+        subs = [(c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
+                 c.block_tables)]
+
+    def step():
+        for a in subs:
+            O.paged_via_sdpa_pt(*a, trim=True)
+
     for _ in range(args.warmup):
-        O.paged_via_sdpa_pt(*a)
+        step()
     ts = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        O.paged_via_sdpa_pt(*a)
+        step()
         ts.append(time.perf_counter() - t0)
-    t = sum(ts) / len(ts)
-    gbs = wl.paged_bytes(c) / t / 1e9
+    t = statistics.median(ts)
+    nbytes = wl.paged_bytes(c)
+    gbs = nbytes / t / 1e9
+    pool = (c.k_cache.numel() + c.v_cache.numel()) * c.k_cache.element_size()
+    cfg = paged_config(name, nbytes, args.gpus, pool) if same else {"workload": WORKLOAD_DESC[name] + " (sample)",
+                                                                   "sample": desc}
     line = {"impl": "reference", "metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3),
+            "us_per_layer_step": round(t * 1e6, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": str(c.dtype).replace("torch.", ""),
-            "data": "synthetic (seeded N(0,1) q/k/v)",
-            "config": {"workload": name, "sample": desc, "cpu_threads": threads},
+            "data": "synthetic (seeded N(0,1) q/k/v, seeded lengths/turns/page permutation)",
+            "config": cfg, "same_config": same,
             "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -362,7 +450,7 @@ def reference_cuda_timing(name):
     so = os.path.join(ROOT, "oracle", "_ref", "dvatt_ref.so")
     if not os.path.exists(so) or not torch.cuda.is_available() or name not in ("config1", "config2", "config3"):
         return None
-    from dvattn_b200 import workloads as wl
+    wl = _wl()
     case = {"config1": wl.config1, "config2": wl.config2, "config3": wl.config3}[name]()
     with tempfile.TemporaryDirectory() as d:
         src, dst = os.path.join(d, "in.pt"), os.path.join(d, "out.pt")
@@ -414,14 +502,10 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     if sampler:
         sampler.begin()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for i in range(args.steps):
-        calls[i % 3]()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    t_ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+    # K steps timed as one rep; reps repeated (>= 25, ~1 s of work) for the clock record
+    # and the spread; value = the median rep
+    per_rep = timed_reps(lambda i: calls[i % 3](), args.steps, world, stream)
+    t_ms = statistics.median(per_rep) / args.steps
 
     # ---- attention kernel alone (roofline), same stream, events between phases ----
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -464,6 +548,14 @@ def run_ours(args, world, rank, local):
     e2e_val = total_bytes / (e2e_ms * 1e-3) / 1e9
     achieved = nbytes / (k_ms * 1e-3) / 1e9
 
+    extra = {}
+    if args.workload == "config2" and not args.no_extra:
+        # strong scaling (same total work at every N): the batch split over the ranks, and
+        # config 3's long context split by KV chunk with its NCCL exchange
+        if world > 1:
+            extra["config2_batch"] = batch_strong_scaling(case, world, rank, args.steps)
+        extra["long3"] = long3_scaling(world, rank, dev, args.steps)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n, sdesc = CPU_SAMPLE[args.workload]
@@ -478,9 +570,10 @@ def run_ours(args, world, rank, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": str(case.dtype).replace("torch.", ""),
             "data": "synthetic (seeded N(0,1) q/k/v, seeded lengths/turns/page permutation)",
-            "config": {"workload": desc, "bytes_per_step_per_gpu": nbytes, "parallelism": f"batch-replica x{world}",
-                       "l2": "inputs larger than L2: 3 rotating KV pools of %.0f MB each" %
-                             ((case.k_cache.numel() + case.v_cache.numel()) * case.k_cache.element_size() / 1e6)},
+            "config": paged_config(args.workload, nbytes, world,
+                                   (case.k_cache.numel() + case.v_cache.numel()) * case.k_cache.element_size()),
+            "timing": dict(spread(per_rep, args.steps), value_from="median rep; each rep = K steps between CUDA "
+                           "events after a barrier and a synchronise, max over ranks"),
             "roofline": {"bound": "hbm", "kernel": "decode_row_kernel" if case.dtype != torch.float32 else
                          "decode_f32_kernel", "achieved": round(achieved, 2), "peak": hbm_peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
@@ -493,10 +586,13 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_layer_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_paged_sdpa", "issue": e2e_mode,
                     "copies": "per step one packed H2D of its inputs and one D2H of its output on copy streams, double-buffered (overlapping the neighbouring steps' ops)"},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": launches_per_step * args.steps * len(per_rep),
+            "gpu_launches_per_step": launches_per_step,
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if extra:
+            line["strong_scaling"] = extra
         print(json.dumps(line), flush=True)
 
 
@@ -895,47 +991,159 @@ def run_views(args, world, rank, local):
             "gpu_launches": args.steps, "clocks": clocks, "cpu_baseline": cpu}), flush=True)
 
 
-def run_long3(args, world, rank, local):
-    """Config 3 with its KV split across the ranks (page-aligned chunks) and the partial
-    outputs merged over NCCL (all-gather of f32 O + LSE, then the LSE-merge kernel)."""
+L2_BYTES = 126 * 1024 * 1024
+
+
+def pool_copies(pool_bytes: int) -> int:
+    """KV pool copies to rotate over so that consecutive steps never find their K/V in L2."""
+    return max(1, min(8, -(-3 * L2_BYTES // max(pool_bytes, 1))))
+
+
+def graph_step_ms(fns, steps: int, world: int, min_reps: int = 25, min_s: float = 0.5):
+    """`steps` calls fns[i % len(fns)]() captured once in a CUDA graph (no host issue cost in
+    the timed region) and replayed: per-rep ms per step (max over ranks), >= min_reps reps."""
+    for i in range(3):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(steps):
+            fns[i % len(fns)]()
+    g.replay()
+    torch.cuda.synchronize()
+    per_rep = timed_reps(lambda k: g.replay(), 1, world, torch.cuda.current_stream(), min_reps, min_s)
+    del g
+    return [x / steps for x in per_rep]
+
+
+def paged_calls(case, n_pools: int, **kw):
+    """PagedCall objects over `n_pools` copies of the case's KV pool (one shared workspace)."""
+    from dvattn_b200 import capi
+    out = case.new_out()
+    calls, ws = [], None
+    for i in range(n_pools):
+        kc = case.k_cache if i == 0 else torch.randn_like(case.k_cache, dtype=torch.float32).to(case.dtype)
+        vc = case.v_cache if i == 0 else torch.randn_like(case.v_cache, dtype=torch.float32).to(case.dtype)
+        c = capi.PagedCall(out, case.scale, case.locations, case.queries, case.cosines, case.sines,
+                           case.fragment_lengths, kc, vc, case.block_tables, workspace=ws, **kw)
+        ws = c.workspace
+        calls.append(c)
+    return calls, out
+
+
+def batch_strong_scaling(case, world: int, rank: int, steps: int) -> dict:
+    """The same batch split over the ranks (dist.balance: LPT on attended keys), each rank
+    holding only its sequences' pages; efficiency against the whole batch on one GPU (every
+    rank times the whole batch alone first).  No collective on the data path."""
+    from dvattn_b200 import dist as ddist
+    wl = _wl()
+    pool_b = (case.k_cache.numel() + case.v_cache.numel()) * case.k_cache.element_size()
+    calls, _ = paged_calls(case, pool_copies(pool_b))
+    t1 = statistics.median(graph_step_ms(calls, steps, world))
+    del calls
+    weights = [int(x) for x in np.asarray(case.turn_lens).sum(axis=1)]
+    bins = ddist.balance(weights, world)
+    sub = ddist.shard_batch(case, bins[rank])
+    sb = (sub.k_cache.numel() + sub.v_cache.numel()) * sub.k_cache.element_size()
+    calls, _ = paged_calls(sub, pool_copies(sb))
+    per = graph_step_ms(calls, steps, world)
+    tn = statistics.median(per)
+    loads = [sum(weights[i] for i in b) for b in bins]
+    return {"us_per_step": round(tn * 1e3, 2), "us_per_step_1gpu": round(t1 * 1e3, 2),
+            "gbs": round(wl.paged_bytes(case) / (tn * 1e-3) / 1e9, 1),
+            "efficiency_vs_1gpu": round(t1 / (world * tn), 4),
+            "sequences_per_rank": [len(b) for b in bins],
+            "max_over_mean_keys": round(max(loads) / (sum(loads) / len(loads)), 4),
+            "timing": "CUDA-graph replay of K steps, median of reps, max over ranks; KV pools rotated past L2"}
+
+
+def long3_scaling(world: int, rank: int, dev: str, steps: int) -> dict:
+    """Config 3 (one 4 x 131072-key fp16 context) split by page-aligned KV chunks over the
+    ranks, each rank keeping only its chunk's pages.  A step = the attention on the chunk
+    (f32 partial O + LSE packed in one buffer), one NCCL all-gather of the packed partials
+    and the LSE merge, captured in a CUDA graph.  Efficiency is against the whole context on
+    one GPU (every rank times it alone first)."""
     from dvattn_b200 import capi, dist as ddist
-    from dvattn_b200 import workloads as wl
-    import torch.distributed as tdist
-    dev = f"cuda:{local}"
-    hbm_peak, _, peak_kind = load_peaks()
+    wl = _wl()
     full = wl.config3(device=dev)
-    nbytes_total = wl.paged_bytes(full)
-    sh = ddist.kv_chunk_shard(full, rank, world)
+    nbytes = wl.paged_bytes(full)
+    calls, _ = paged_calls(full, 1)
+    t1 = statistics.median(graph_step_ms(calls, steps, world))
+    del calls
+    if world == 1:
+        del full
+        torch.cuda.empty_cache()
+        return {"us_per_step": round(t1 * 1e3, 2), "gbs": round(nbytes / (t1 * 1e-3) / 1e9, 1),
+                "parallelism": "kv-chunk x1 (no exchange)"}
+    sh = ddist.kv_chunk_shard(full, rank, world, local_pages=True)
+    del full
+    torch.cuda.empty_cache()
     out = sh.new_out()
-    # f32 partial outputs and LSEs in one buffer: one all-gather per step
     packed, o32, lse = ddist.packed_partials(out)
-    call = capi.PagedCall(*sh.op_args(out), lse=lse, out_f32=o32)
+    gathered = ddist.gather_buffer(packed)
     merged = torch.empty_like(out)
+    pb = (sh.k_cache.numel() + sh.v_cache.numel()) * sh.k_cache.element_size()
+    calls, _ = paged_calls(sh, pool_copies(pb), lse=lse, out_f32=o32)
+    import torch.distributed as tdist
+    Ev = out.size(-1)
+    rows = out.numel() // Ev
 
-    def step():
-        call()
-        if world > 1:
-            ddist.allgather_merge_packed(packed, merged)
+    def step_fn(c):
+        def f():
+            c()
+            ddist.allgather_merge_packed(packed, merged, gathered=gathered)
+        return f
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
-    value = nbytes_total / (t_ms * 1e-3) / 1e9
+    def attend_fn(c):
+        return lambda: c()
+
+    def exchange():
+        tdist.all_gather_into_tensor(gathered, packed)
+
+    def merge():
+        capi.lse_merge_packed(gathered.view(world, rows * (Ev + 1)), merged)
+
+    mode = "cuda-graph"
+    try:
+        tn = statistics.median(graph_step_ms([step_fn(c) for c in calls], steps, world))
+        t_att = statistics.median(graph_step_ms([attend_fn(c) for c in calls], steps, world))
+        t_ex = statistics.median(graph_step_ms([exchange], steps, world))
+        t_mg = statistics.median(graph_step_ms([merge], steps, world))
+    except Exception as e:  # a collective that cannot be captured: time eagerly
+        mode = "eager (%s)" % str(e).splitlines()[0][:80]
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        fs = [step_fn(c) for c in calls]
+        tn = statistics.median(timed_reps(lambda k: fs[k % len(fs)](), steps, world, st)) / steps
+        fa = [attend_fn(c) for c in calls]
+        t_att = statistics.median(timed_reps(lambda k: fa[k % len(fa)](), steps, world, st)) / steps
+        t_ex = statistics.median(timed_reps(lambda k: exchange(), steps, world, st)) / steps
+        t_mg = statistics.median(timed_reps(lambda k: merge(), steps, world, st)) / steps
+    return {"us_per_step": round(tn * 1e3, 2), "us_per_step_1gpu": round(t1 * 1e3, 2),
+            "gbs": round(nbytes / (tn * 1e-3) / 1e9, 1), "efficiency_vs_1gpu": round(t1 / (world * tn), 4),
+            "attention_us": round(t_att * 1e3, 2), "exchange_us": round(t_ex * 1e3, 2),
+            "merge_us": round(t_mg * 1e3, 2), "exchange_bytes_per_rank": packed.numel() * 4,
+            "parallelism": f"kv-chunk x{world}, local pages only", "issue": mode,
+            "timing": "per step: attention + NCCL all_gather_into_tensor + dvattn_lse_merge_packed; median of "
+                      "reps, max over ranks; the parts timed alone the same way"}
+
+
+def run_long3(args, world, rank, local):
+    """Config 3 with its KV split across the ranks (page-aligned chunks, local pages) and
+    the partial outputs merged over NCCL (one all-gather of the packed f32 O + LSE, then the
+    LSE-merge kernel), one JSON line."""
+    dev = f"cuda:{local}"
+    wl = _wl()
+    r = long3_scaling(world, rank, dev, args.steps)
     if rank == 0:
-        print(json.dumps({"metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+        t_ms = r["us_per_step"] / 1e3
+        print(json.dumps({"metric": METRIC, "value": r["gbs"], "unit": "GB/s", "n_gpus": world,
                           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 5),
                           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "float16",
-                          "data": "synthetic", "config": {"workload": "config3 KV-chunk sharded + one NCCL all-gather + LSE merge",
+                          "data": "synthetic", "config": {"workload": "config3 KV-chunk sharded + one NCCL all-gather "
+                                                                      "+ LSE merge",
                                                           "parallelism": f"kv-chunk x{world}"},
-                          "gpu_launches": args.steps * (3 + (1 if world > 1 else 0))}), flush=True)
+                          "long3": r, "gpu_launches": args.steps * (3 + (1 if world > 1 else 0))}), flush=True)
 
 
 def main():
@@ -949,6 +1157,7 @@ def main():
                              "views4"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-ref-cuda", action="store_true", help="reference arm: skip timing the reference CUDA op")
+    ap.add_argument("--no-extra", action="store_true", help="skip the strong-scaling legs of the default workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

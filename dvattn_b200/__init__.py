@@ -2,9 +2,9 @@
 
 Importing the package loads ``dvatt.abi3.so``, which registers the reference's
 ``torch.ops.libdvatt`` schemas (``dvattn_paged_sdpa``, ``dvattn_varlen_paged_sdpa``,
-``dvattn_rope``, ``dvattn_varlen_rope``; ``dvattn_sdpa`` / ``dvattn_fused`` are registered
-but raise) plus the B200 additions ``dvattn_paged_sdpa_ex``, ``dvattn_varlen_paged_sdpa_ex``
-and ``dvattn_lse_merge``.  There is no CPU fallback: if the native libraries are missing,
+``dvattn_rope``, ``dvattn_varlen_rope``, ``dvattn_sdpa``, ``dvattn_fused``) plus the B200
+additions (``dvattn_paged_sdpa_ex``, ``dvattn_varlen_paged_sdpa_ex``, ``dvattn_lse_merge``,
+``dvattn_paged_append``, ``dvattn_build_views`` and the ``*_rope`` attention variants).  There is no CPU fallback: if the native libraries are missing,
 the import fails.
 """
 from __future__ import annotations

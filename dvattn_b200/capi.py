@@ -43,6 +43,7 @@ EXPORTS = [
     "dvattn_varlen_paged_sdpa_phase",
     "dvattn_paged_sdpa_noalloc_max_workspace",
     "dvattn_paged_sdpa_noalloc",
+    "dvattn_workspace_status",
     "dvattn_varlen_paged_sdpa_workspace_size",
     "dvattn_varlen_paged_sdpa",
     "dvattn_rope",
@@ -135,6 +136,8 @@ def lib() -> ctypes.CDLL:
         L.dvattn_paged_sdpa_noalloc_max_workspace.argtypes = []
         L.dvattn_paged_sdpa_noalloc.restype = _i
         L.dvattn_paged_sdpa_noalloc.argtypes = [ctypes.POINTER(PagedArgs), _vp]
+        L.dvattn_workspace_status.restype = _i
+        L.dvattn_workspace_status.argtypes = [_vp, _vp, ctypes.POINTER(_i)]
         L.dvattn_varlen_paged_sdpa_workspace_size.restype = ctypes.c_size_t
         L.dvattn_varlen_paged_sdpa_workspace_size.argtypes = [ctypes.POINTER(VarlenArgs)]
         L.dvattn_varlen_paged_sdpa.restype = _i
@@ -244,6 +247,10 @@ class PagedCall:
         if st != DVATTN_OK:
             raise DvattnError(st, "dvattn_paged_sdpa")
 
+    def status(self, stream: Optional[torch.cuda.Stream] = None) -> int:
+        """Error word of the last launch on this call's workspace (0 = completed)."""
+        return workspace_status(self.workspace, stream)
+
     def phase(self, phase: int, stream: Optional[torch.cuda.Stream] = None) -> None:
         st = lib().dvattn_paged_sdpa_phase(ctypes.byref(self.args), self.workspace.data_ptr(),
                                            self.workspace.numel(), phase, _stream(stream))
@@ -269,11 +276,27 @@ class VarlenCall:
         if st != DVATTN_OK:
             raise DvattnError(st, "dvattn_varlen_paged_sdpa")
 
+    def status(self, stream: Optional[torch.cuda.Stream] = None) -> int:
+        """Error word of the last launch on this call's workspace (0 = completed)."""
+        return workspace_status(self.workspace, stream)
+
     def phase(self, phase: int, stream: Optional[torch.cuda.Stream] = None) -> None:
         st = lib().dvattn_varlen_paged_sdpa_phase(ctypes.byref(self.args), self.workspace.data_ptr(),
                                                   self.workspace.numel(), phase, _stream(stream))
         if st != DVATTN_OK:
             raise DvattnError(st, "dvattn_varlen_paged_sdpa_phase")
+
+
+def workspace_status(workspace: Optional[torch.Tensor] = None, stream: Optional[torch.cuda.Stream] = None) -> int:
+    """dvattn_workspace_status: the error word of the last attention call on `workspace`
+    (None: the last dvattn_paged_sdpa_noalloc call on the current device).  0 = completed;
+    nonzero = a bounded wait in a kernel gave up and that call's outputs are invalid.
+    Waits for the stream."""
+    word = _i(0)
+    st = lib().dvattn_workspace_status(_ptr(workspace), _stream(stream), ctypes.byref(word))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_workspace_status")
+    return word.value
 
 
 def paged_sdpa(out, scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,

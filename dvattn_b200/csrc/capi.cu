@@ -18,6 +18,22 @@ const char* dvattn_status_string(int status) {
 
 size_t dvattn_paged_sdpa_workspace_size(const dvattn_paged_args* args) { return dvb::decode_workspace_size(args); }
 
+int dvattn_workspace_status(const void* workspace, dvattn_stream_t stream, int* error_word) {
+    if (!error_word) return DVATTN_ERR_INVALID_ARGUMENT;
+    *error_word = 0;
+    void* ws = const_cast<void*>(workspace);
+    if (!ws && dvb::noalloc_scratch(&ws) != DVATTN_OK) return DVATTN_ERR_CUDA;
+    if (reinterpret_cast<uintptr_t>(ws) & 255) return DVATTN_ERR_WORKSPACE;
+    int word = 0;
+    const cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemcpyAsync(&word, static_cast<const char*>(ws) + dvb::kErrorWordOffset, sizeof(int),
+                        cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+        return DVATTN_ERR_CUDA;
+    *error_word = word;
+    return DVATTN_OK;
+}
+
 int dvattn_paged_sdpa(const dvattn_paged_args* args, void* workspace, size_t workspace_bytes, dvattn_stream_t stream) {
     return dvb::decode_launch(args, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
                               DVATTN_PHASE_ALL);

@@ -20,22 +20,6 @@
 
 namespace dvb {
 
-// Scratch instrumentation: compiled only with -DDVB_TRACE (never in the product build).
-#ifdef DVB_TRACE
-__device__ unsigned long long g_trace[12][4096];
-}  // namespace dvb
-extern "C" void dvb_trace_read(unsigned long long* h) { cudaMemcpyFromSymbol(h, dvb::g_trace, sizeof(dvb::g_trace)); }
-extern "C" void dvb_trace_clear() {
-    static unsigned long long z[12][4096];
-    cudaMemcpyToSymbol(dvb::g_trace, z, sizeof(z));
-}
-namespace dvb {
-#define DVB_TC(k) do { if (blockIdx.x < 4096) g_trace[k][blockIdx.x] = global_ns(); } while (0)
-#define DVB_TADD(k, v) do { if (blockIdx.x < 4096) atomicAdd(&g_trace[k][blockIdx.x], (unsigned long long)(v)); } while (0)
-#else
-#define DVB_TC(k) do { } while (0)
-#define DVB_TADD(k, v) do { } while (0)
-#endif
 
 // ----------------------------------------------------------------------------------
 // query rotation of one (row ws, KV head, turn f) into shared memory.
@@ -104,9 +88,6 @@ __device__ __forceinline__ void rotate_q_rows(const PagedParams& p, int ws, int 
             }
         }
         named_bar_sync(bar_id, nth);
-#ifdef DVB_TRACE
-        if (tid == 0) DVB_TADD(5, global_ns());
-#endif
 #pragma unroll
         for (int k = 0; k < MAXT; ++k) {
             const int t = tid + k * nth;
@@ -986,7 +967,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    if (tid == 0) DVB_TC(0);
     const int Hkv = p.Hkv;
     const int TOKB = (CW / Hkv) * 16;           // keys per stage (window)
     // One TMA box = one page (or the window's part of it) for all heads and panels:
@@ -1117,6 +1097,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                 }
                 break;
             }
+            if (i == p.stall_tile && c == 0) continue;  // test hook: this stage is never filled
             const TileDesc& d = cur.d;
             const int win = d.pos0 & ~(TOKB - 1);
             if (lane == 0) {
@@ -1219,12 +1200,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             }
             continue;
         }
-        if (tid == 0 && i == 0) DVB_TC(1);
         const StageDesc d = sDesc[st];
-        if (d.n < 0) {
-            if (tid == 0) DVB_TC(2);
-            break;
-        }
+        if (d.n < 0) break;
         if (d.flags & 1) {
             m0 = m1 = neg_inf();
             l0 = l1 = 0.f;
@@ -1232,10 +1209,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             for (int j = 0; j < E / 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
         }
         if ((d.flags & 2) && i > 0) {
-#ifdef DVB_TRACE
-            const unsigned long long tr0 = global_ns();
-            if (tid == 0) DVB_TADD(6, tr0);
-#endif
             named_bar_sync(2, CW * 32);
             rotate_q_inplace<T, E>(p, d.ws, d.f, Hkv, sQ, tid, CW * 32,
                                                                            reinterpret_cast<float*>(smem + C::OFF_CS), 2);
@@ -1248,9 +1221,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
                             qf[kk][2], qf[kk][3]);
                 }
             }
-#ifdef DVB_TRACE
-            if (tid == 0) { DVB_TADD(3, global_ns() - tr0); DVB_TADD(4, 1); }
-#endif
         }
 
         const int lo = max(0, d.r0 - rb), hi = min(16, d.r0 + d.n - rb);
@@ -1769,10 +1739,8 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     constexpr int NTH = 16 * (E / 4);
     // launched as a programmatic dependent of the attention kernel: wait for its results
     // let the next call's schedule kernel start its (read-only) work now
-    if (threadIdx.x == 0) DVB_TC(8);
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (threadIdx.x == 0) DVB_TC(9);
     const int tid = threadIdx.x;
     // The CTA boundaries are searched twice below: stage them in shared memory with one
     // round of parallel loads instead of a chain of dependent global loads.
@@ -1782,15 +1750,27 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
     if (cs_shared)
         for (int i = tid; i <= p.n_launch; i += NTH) s_cs[i] = p.cstart[i];
     const DecodeSched sch = *p.sched;
+    if (sch.error) {
+        // a bounded wait of the attention kernel gave up: every output of the call is
+        // marked invalid (NaN) rather than merged from pieces that may be missing
+        const float nan = __int_as_float(0x7fc00000);
+        for (int g_seg = blockIdx.x; g_seg < p.WS * p.Hkv; g_seg += gridDim.x) {
+            const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
+            const int r = tid / (E / 4), c4 = tid - r * (E / 4);
+            if (r >= p.gqa) continue;
+            const int w = ws / p.S, s = ws - w * p.S;
+            const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
+            store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, nan, nan, nan, nan);
+            if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = make_float4(nan, nan, nan, nan);
+            if (p.lse_out && c4 == 0) p.lse_out[orow] = nan;
+        }
+        return;
+    }
     __syncthreads();
     const long long* cst = cs_shared ? s_cs : p.cstart;
     __shared__ int s_part[NTH];
     for (int g_seg = blockIdx.x; g_seg < p.WS * p.Hkv; g_seg += gridDim.x)
         merge_segment<T, E>(p, g_seg, cst, sch.n_eff, s_part);
-#ifdef DVB_TRACE
-    __syncthreads();
-    if (threadIdx.x == 0) DVB_TC(10);
-#endif
 }
 
 // ==================================================================================
@@ -2040,6 +2020,17 @@ static bool pdl_enabled() {
     return on;
 }
 
+// DVATTN_TEST_STALL_TILE=<i>: tests only.  CTA 0 of the row kernel skips the loads of its
+// tile i, so the consumers' bounded wait runs out (after ~2 s) and the call's error word
+// is set; read once per process.
+static int stall_tile_hook() {
+    static const int t = [] {
+        const char* e = getenv("DVATTN_TEST_STALL_TILE");
+        return e && *e ? atoi(e) : -1;
+    }();
+    return t;
+}
+
 static bool first_launch_may_overlap(int dev, cudaStream_t s, const Span* in, int nin) {
     if (!pdl_enabled()) return false;
     std::lock_guard<std::mutex> lk(g_last_mu);
@@ -2169,6 +2160,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     // prep kernel runs and a call's streaming starts while the previous call's merge runs.
     p.fused = (kc.row && !p.cu_q && (size_t)(p.WS + 1 + 32) * 8 <= kc.sched_smem &&
                (long long)p.WS + 1 <= 32LL * n_launch) ? 1 : 0;
+    p.stall_tile = stall_tile_hook();
 
     // the first kernel this call launches may overlap the kernel before it only if that
     // kernel cannot have written this call's inputs (see first_launch_may_overlap)

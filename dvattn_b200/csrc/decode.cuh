@@ -6,6 +6,10 @@
 
 namespace dvb {
 
+// The error word sits at this byte offset of every attention workspace (DecodeSched of
+// the decode header, header[3] of the prefill); dvattn_workspace_status reads it.
+constexpr size_t kErrorWordOffset = 12;
+
 int decode_validate(const dvattn_paged_args* a);
 size_t decode_workspace_size(const dvattn_paged_args* a);
 int decode_launch(const dvattn_paged_args* a, void* workspace, size_t wbytes, cudaStream_t stream, int phase);
@@ -37,6 +41,9 @@ int varlen_rope_launch(int dtype, int F, int T, int H, int E, int R, void* out, 
                        const float* sin, cudaStream_t stream);
 int lse_merge_launch(int dtype, int num_parts, long long rows, int Ev, const float* part_out, const float* part_lse,
                      void* out, float* lse_out, cudaStream_t stream);
+// device address of the no-alloc scratch on the current device (noalloc.cu)
+int noalloc_scratch(void** out);
+
 int lse_merge_packed_launch(int dtype, int parts, long long rows, int Ev, const float* packed, void* out,
                             float* lse_out, cudaStream_t stream);
 

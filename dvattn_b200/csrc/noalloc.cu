@@ -23,7 +23,10 @@ constexpr int kMaxDevices = 64;
 void* g_scratch_ptr[kMaxDevices] = {};
 std::mutex g_scratch_mu;
 
-int scratch_for_current_device(void** out) {
+}  // namespace
+
+namespace dvb {
+int noalloc_scratch(void** out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return DVATTN_ERR_CUDA;
     std::lock_guard<std::mutex> lk(g_scratch_mu);
@@ -35,8 +38,7 @@ int scratch_for_current_device(void** out) {
     *out = g_scratch_ptr[dev];
     return DVATTN_OK;
 }
-
-}  // namespace
+}  // namespace dvb
 
 extern "C" size_t dvattn_paged_sdpa_noalloc_max_workspace(void) { return kScratchBytes; }
 
@@ -48,7 +50,7 @@ extern "C" int dvattn_paged_sdpa_noalloc(const dvattn_paged_args* args, dvattn_s
     if (need == 0) return DVATTN_ERR_CUDA;
     if (need > kScratchBytes) return DVATTN_ERR_WORKSPACE;  // problem too large for the fixed scratch
     void* ws = nullptr;
-    st = scratch_for_current_device(&ws);
+    st = dvb::noalloc_scratch(&ws);
     if (st != DVATTN_OK) return st;
     // Nothing in the scratch needs to start at zero: the schedule phase rewrites the
     // header and prefix sums, and every partial is written before it is read.

@@ -70,8 +70,9 @@ struct Params {
     float* lse_out;
     float* out_f32;
     Item* items;
-    int* header;  // [0] item count, [1] error word
+    int* header;  // [0] item count, [3] error word (byte offset kErrorWordOffset, as in decode)
     int max_items;
+    int stall_tile;  // test hook (DVATTN_TEST_STALL_TILE): CTA 0 never loads this K window; -1: off
 };
 
 // ---- tcgen05 helpers -------------------------------------------------------------
@@ -242,7 +243,7 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(Params p) {
             acc += (sb[s] - sa[s] + p.tpi - 1) / p.tpi * p.Hkv;
         }
         p.header[0] = acc < p.max_items ? acc : p.max_items;
-        p.header[1] = 0;
+        p.header[3] = 0;
     }
     __syncthreads();
     for (int s = tid; s < NS; s += 1024) {
@@ -253,26 +254,6 @@ __global__ void __launch_bounds__(1024) prefill_prep_kernel(Params p) {
                 if (k < p.max_items) p.items[k] = Item{s < p.W ? s : 0, a + q * p.tpi, min(p.tpi, b - a - q * p.tpi), h};
     }
 }
-
-// Scratch instrumentation: compiled only with -DPF_TRACE (never in the product build).
-#ifdef PF_TRACE
-__device__ unsigned long long g_pf_trace[256 * 32];
-#define PF_TR(i, slot) \
-    do { \
-        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (i) < 256) g_pf_trace[(i) * 32 + (slot)] = clock64(); \
-    } while (0)
-}  // namespace pf
-}  // namespace dvb
-extern "C" void dvb_pf_trace_read(unsigned long long* h) {
-    cudaMemcpyFromSymbol(h, dvb::pf::g_pf_trace, sizeof(dvb::pf::g_pf_trace));
-}
-namespace dvb {
-namespace pf {
-#else
-#define PF_TR(i, slot) \
-    do { \
-    } while (0)
-#endif
 
 // Waits of the producer and MMA warps: a poll every ~100 ns instead of a tight try_wait
 // loop, so the two softmax warps on the same SM sub-partitions get the issue slots
@@ -344,7 +325,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const uint32_t s0 = smem_u32(smem);
     if (s0 & 1023) {
-        if (tid == 0) atomicOr(p.header + 1, 4);
+        if (tid == 0) atomicOr(p.header + 3, 4);
         return;
     }
     if ((int)blockIdx.x >= p.header[0]) return;
@@ -423,8 +404,8 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                     ok = false;
                     break;
                 }
-                PF_TR(ik, 0);
-                load(kq, &tmk, s0 + (uint32_t)(OFF_K + ks * TILE), k_full + 8 * ks);
+                if (!(ik == p.stall_tile && blockIdx.x == 0))  // test hook: this window never lands
+                    load(kq, &tmk, s0 + (uint32_t)(OFF_K + ks * TILE), k_full + 8 * ks);
                 kq.next(p, it, lane);
                 ++ik;
             }
@@ -434,14 +415,20 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                 ok = false;
                 break;
             }
-            PF_TR(iv, 11);
             load(vq, &tmv, s0 + (uint32_t)(OFF_V + vs * TILE), v_full + 8 * vs);
             vq.next(p, it, lane);
             ++iv;
         }
-        if (!ok && lane == 0) {
-            *sAbort = 1;
-            atomicOr(p.header + 1, 1);
+        if (!ok) {
+            if (lane == 0) {
+                *sAbort = 1;
+                atomicOr(p.header + 3, 1);
+            }
+            // the windows already requested land before the CTA can exit (bounded waits)
+            for (int j = ik > KSTAGES ? ik - KSTAGES : 0; j < ik; ++j)
+                mbar_wait(k_full + 8 * (j % KSTAGES), (j / KSTAGES) & 1);
+            for (int j = iv > VSTAGES ? iv - VSTAGES : 0; j < iv; ++j)
+                mbar_wait(v_full + 8 * (j & 1), (j >> 1) & 1);
         }
     } else if (wid == WARP_MMA) {
         // ================================ MMA ================================
@@ -489,31 +476,23 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             const int ks = i % KSTAGES, vs = i & 1;
             const bool first = ts.first();
             if (!mbar_wait_lazy(k_full + 8 * ks, (i / KSTAGES) & 1)) { ok = false; break; }
-            PF_TR(i, 1);
             if (first && !mbar_wait_lazy(q_ready, turn & 1)) { ok = false; break; }
             tc_fence_after();
             issue_s(0, ks);
-            PF_TR(i, 18);
             if (i > 0) {
                 if (!mbar_wait_lazy(p_full + 8, (i - 1) & 1)) { ok = false; break; }
-                PF_TR(i - 1, 2);
                 tc_fence_after();
                 issue_pv(1, vs ^ 1, i - 1 > 0);
                 commit(v_empty + 8 * (vs ^ 1));
-                PF_TR(i, 19);
             }
             if (first && !mbar_wait_lazy(q_ready + 8, turn & 1)) { ok = false; break; }
             tc_fence_after();
             issue_s(1, ks);
             commit(k_empty + 8 * ks);
-            PF_TR(i, 20);
             if (!mbar_wait_lazy(v_full + 8 * vs, (i >> 1) & 1)) { ok = false; break; }
-            PF_TR(i, 15);
             if (!mbar_wait_lazy(p_full, i & 1)) { ok = false; break; }
-            PF_TR(i, 3);
             tc_fence_after();
             issue_pv(0, vs, i > 0);
-            PF_TR(i, 16);
             if (first) ++turn;
         }
         if (ok && i > 0) {
@@ -526,7 +505,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
         }
         if (!ok && lane == 0) {
             *sAbort = 1;
-            atomicOr(p.header + 1, 2);
+            atomicOr(p.header + 3, 2);
         }
         // o_done: every MMA of the item has completed (the epilogue and the TMEM release
         // wait on it)
@@ -599,14 +578,12 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             {
                 {
                     if (!mbar_wait(s_full + 8 * grp, i & 1)) { ok = false; break; }
-                    if ((wid & 3) == 0) PF_TR(i, 4 + 2 * grp);
                     tc_fence_after();
                     float sv[KT];
 #pragma unroll
                     for (int c = 0; c < KT / 32; ++c) tmem_ld32(tS + 32 * c, *reinterpret_cast<float(*)[32]>(sv + 32 * c));
                     tmem_wait_ld();
                     reg_fence<KT>(sv);
-                    if ((wid & 3) == 0) PF_TR(i, 8 + 4 * grp);
                     const int lo = off - win, hi = lim - win;  // visible columns [lo, hi]
                     if (!__all_sync(0xffffffffu, lo <= 0 && hi >= KT - 1)) {
 #pragma unroll
@@ -652,7 +629,6 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                     }
                     l = l * alpha + psum;
                     m = mnew;
-                    if ((wid & 3) == 0) PF_TR(i, 9 + 4 * grp);
                     if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
                         // O holds the PV of every earlier window (their MMAs completed
                         // before S of this window was signalled)
@@ -667,7 +643,6 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                             tmem_st32(tO + 32 * c, ov);
                         }
                     }
-                    if ((wid & 3) == 0) PF_TR(i, 10 + 4 * grp);
                     if (grp == 0 && (win < off || win + KT > vend)) {
                         // V rows of this window outside [off, vend) may hold another turn's
                         // or uninitialised pool data: zero them (P is 0 there, 0 * NaN is NaN)
@@ -685,14 +660,13 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
                     }
                     tmem_wait_st();
                     tc_fence_before();
-                    if ((wid & 3) == 0) PF_TR(i, 5 + 2 * grp);
                     mbar_arrive(p_full + 8 * grp);
                 }
             }
         }
         if (!ok && lane == 0) {
             *sAbort = 1;
-            atomicOr(p.header + 1, 8);
+            atomicOr(p.header + 3, 8);
         }
         // ---- epilogue: O / l -> output ----
         const bool done = mbar_wait(o_done, 0);
@@ -728,7 +702,18 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             }
             if (row_ok && p.lse_out) p.lse_out[(size_t)t * p.Hq + hq] = l > 0.f ? (m + __log2f(l)) * kLn2 : neg_inf();
         }
-        if (row_ok && i == 0) {  // no visible key at all: zeros
+        if (row_ok && !(ok && done)) {
+            // this item gave up on a bounded wait: its rows are marked invalid (NaN)
+            const float nan = __int_as_float(0x7fc00000);
+            T* op = static_cast<T*>(p.out) + ((size_t)t * p.Hq + hq) * E;
+            const uint32_t hn = Elem<T>::pack2(nan, nan);
+            for (int c = 0; c < E; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(hn, hn, hn, hn);
+            if (p.out_f32)
+                for (int c = 0; c < E; c += 4)
+                    *reinterpret_cast<float4*>(p.out_f32 + ((size_t)t * p.Hq + hq) * E + c) = make_float4(nan, nan, nan, nan);
+            if (p.lse_out) p.lse_out[(size_t)t * p.Hq + hq] = nan;
+        }
+        if (row_ok && ok && done && i == 0) {  // no visible key at all: zeros
             T* op = static_cast<T*>(p.out) + ((size_t)t * p.Hq + hq) * E;
             for (int c = 0; c < E; c += 8) *reinterpret_cast<uint4*>(op + c) = make_uint4(0u, 0u, 0u, 0u);
             if (p.out_f32)
@@ -775,6 +760,15 @@ bool prefill_eligible(const dvattn_varlen_args* v) {
     return mode == 1 || (long long)v->T * v->Hkv >= 148LL * prefill_tokens_per_item(v);
 }
 
+// DVATTN_TEST_STALL_TILE=<i>: tests only (see the decode launcher); read once per process.
+static int prefill_stall_hook() {
+    static const int t = [] {
+        const char* e = getenv("DVATTN_TEST_STALL_TILE");
+        return e && *e ? atoi(e) : -1;
+    }();
+    return t;
+}
+
 static int prefill_max_items(const dvattn_varlen_args* v) {
     return (v->T / prefill_tokens_per_item(v) + v->W + 1) * v->Hkv;
 }
@@ -800,6 +794,7 @@ int prefill_launch(const dvattn_varlen_args* v, void* workspace, size_t wbytes, 
     p.header = static_cast<int*>(workspace);
     p.items = reinterpret_cast<pf::Item*>(static_cast<char*>(workspace) + 256);
     p.max_items = prefill_max_items(v);
+    p.stall_tile = prefill_stall_hook();
 
     const size_t prep_smem = (sizeof(long long) + 4 * sizeof(int)) * ((size_t)p.W + 1);
     if (prep_smem > 48 * 1024) return DVATTN_ERR_UNSUPPORTED;

@@ -37,6 +37,7 @@ struct DecodeSched {
     int n_eff;    // CTAs that own units (<= n_launch)
     int error;    // nonzero: a bounded wait gave up (the outputs of this call are invalid)
 };
+static_assert(offsetof(DecodeSched, error) == 12, "the error word is read at byte 12 (kErrorWordOffset)");
 
 // Device-side view of one paged decode call (passed by value).
 struct PagedParams {
@@ -86,6 +87,9 @@ struct PagedParams {
     // row kernel on fragments: 2 * nfrag 128-byte tensor maps (K then V of each turn) in
     // the workspace
     const char* fmaps;
+    // Test hook (DVATTN_TEST_STALL_TILE): the row kernel's CTA 0 never issues the loads of
+    // this tile, so a bounded wait runs out and the call reports its error word; -1: off.
+    int stall_tile;
 };
 
 

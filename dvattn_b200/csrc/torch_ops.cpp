@@ -29,6 +29,25 @@ void check_status(int st, const char* what) {
     TORCH_CHECK(st == DVATTN_OK, "dvattn: ", what, " failed: ", dvattn_status_string(st));
 }
 
+// DVATTN_CHECK_STATUS=1: after every attention call, wait for the stream and raise if a
+// bounded wait inside a kernel gave up (dvattn_workspace_status).  Off by default: the
+// check synchronises the stream.
+bool check_status_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("DVATTN_CHECK_STATUS");
+        return e && e[0] && e[0] != '0';
+    }();
+    return on;
+}
+
+void check_call_status(const at::Tensor& ws, dvattn_stream_t stream, const char* what) {
+    if (!check_status_enabled()) return;
+    int word = 0;
+    check_status(dvattn_workspace_status(ws.data_ptr(), stream, &word), what);
+    TORCH_CHECK(word == 0, "dvattn: ", what, ": a bounded wait in the kernel gave up (error word ", word,
+                "); the outputs of this call are invalid");
+}
+
 void check_cuda_tensor(const at::Tensor& t, const char* name, const at::Tensor& out) {
     TORCH_CHECK(t.is_cuda(), "dvattn: ", name, " must be a CUDA tensor");
     TORCH_CHECK(t.device() == out.device(), "dvattn: ", name, " is on ", t.device(), " but output is on ", out.device());
@@ -155,6 +174,7 @@ void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, cons
         TORCH_CHECK(wsb > 0, "dvattn_paged_sdpa_rope: could not size the workspace (unsupported or invalid shape)");
         at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
         check_status(dvattn_paged_sdpa_rope(&a, &ra, ws.data_ptr(), wsb, cur_stream(out)), "dvattn_paged_sdpa_rope");
+        check_call_status(ws, cur_stream(out), "dvattn_paged_sdpa_rope");
         return;
     }
     int st = dvattn_paged_sdpa(&a, nullptr, 0, cur_stream(out));  // validation only when nothing to do
@@ -163,6 +183,8 @@ void paged_impl(at::Tensor& out, double scale, const at::Tensor& locations, cons
         TORCH_CHECK(wsb > 0, "dvattn_paged_sdpa: could not size the workspace");
         at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
         st = dvattn_paged_sdpa(&a, ws.data_ptr(), wsb, cur_stream(out));
+        check_status(st, "dvattn_paged_sdpa");
+        check_call_status(ws, cur_stream(out), "dvattn_paged_sdpa");
     }
     check_status(st, "dvattn_paged_sdpa");
 }
@@ -263,6 +285,7 @@ void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, con
         at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
         check_status(dvattn_varlen_paged_sdpa_rope(&a, &ra, ws.data_ptr(), wsb, cur_stream(out)),
                      "dvattn_varlen_paged_sdpa_rope");
+        check_call_status(ws, cur_stream(out), "dvattn_varlen_paged_sdpa_rope");
         return;
     }
     int st = dvattn_varlen_paged_sdpa(&a, nullptr, 0, cur_stream(out));
@@ -271,6 +294,8 @@ void varlen_impl(at::Tensor& out, double scale, const at::Tensor& locations, con
         TORCH_CHECK(wsb > 0, "dvattn_varlen_paged_sdpa: could not size the workspace");
         at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
         st = dvattn_varlen_paged_sdpa(&a, ws.data_ptr(), wsb, cur_stream(out));
+        check_status(st, "dvattn_varlen_paged_sdpa");
+        check_call_status(ws, cur_stream(out), "dvattn_varlen_paged_sdpa");
     }
     check_status(st, "dvattn_varlen_paged_sdpa");
 }
@@ -547,6 +572,8 @@ void sdpa_impl(at::Tensor& out, double scale, const at::Tensor& locations, const
         TORCH_CHECK(wsb > 0, name, ": could not size the workspace");
         at::Tensor ws = at::empty({(int64_t)wsb}, out.options().dtype(at::kByte));
         st = dvattn_sdpa(&a, ws.data_ptr(), wsb, cur_stream(out));
+        check_status(st, name);
+        check_call_status(ws, cur_stream(out), name);
     }
     check_status(st, name);
 }

@@ -48,11 +48,44 @@ def kv_chunk_bounds(total: int, block_size: int, n: int) -> List[Tuple[int, int]
     return out
 
 
-def kv_chunk_shard(case: PagedCase, rank: int, world: int) -> PagedCase:
+def compact_pages(k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor):
+    """A pool holding only the pages `block_tables` references, and the table renumbered
+    into it.  Entries outside [0, NB) stay outside (-1), so they still read as zeros."""
+    NB = k_cache.size(0)
+    bt = block_tables.to(torch.int64)
+    valid = (bt >= 0) & (bt < NB)
+    used = torch.unique(bt[valid])
+    lookup = torch.full((NB,), -1, dtype=torch.int64, device=bt.device)
+    lookup[used] = torch.arange(used.numel(), device=bt.device)
+    new_bt = torch.where(valid, lookup[bt.clamp(0, max(NB - 1, 0))], torch.full_like(bt, -1))
+    idx = used.to(k_cache.device)
+    return k_cache[idx].contiguous(), v_cache[idx].contiguous(), new_bt.to(torch.int32).contiguous()
+
+
+def shard_batch(case: PagedCase, seqs: Sequence[int]) -> PagedCase:
+    """The sequences `seqs` of a paged decode case as a case of their own, with a page pool
+    holding only their pages (what the rank that owns them keeps in memory).  Turn lengths
+    stay global (they place the turns in every sequence's logical positions)."""
+    dev = case.queries.device
+    idx = torch.as_tensor(list(seqs), dtype=torch.int64, device=dev)
+    S = case.queries.size(2)
+    kc, vc, bt = compact_pages(case.k_cache, case.v_cache, case.block_tables.index_select(0, idx))
+    return PagedCase(queries=case.queries.index_select(0, idx).contiguous(),
+                     locations=case.locations.index_select(1, idx).contiguous(),
+                     cosines=case.cosines.index_select(1, idx).contiguous(),
+                     sines=case.sines.index_select(1, idx).contiguous(),
+                     fragment_lengths=case.fragment_lengths.clone(), k_cache=kc, v_cache=vc, block_tables=bt,
+                     scale=case.scale,
+                     turn_lens=None if case.turn_lens is None else case.turn_lens[list(seqs)],
+                     meta=dict(case.meta, seqs=list(seqs), S=S))
+
+
+def kv_chunk_shard(case: PagedCase, rank: int, world: int, local_pages: bool = False) -> PagedCase:
     """The slice of a single-turn paged case that rank `rank` of `world` attends over.
     Keys keep their rotation (it is relative to the turn start, which does not move);
     locations shift by the chunk start, so key l of the chunk is visible iff
-    a + l <= loc.  The page pool is shared (views)."""
+    a + l <= loc.  local_pages=False shares the page pool (views); True gives the shard a
+    pool of only the pages of its chunk (what the rank keeps in memory)."""
     F = case.locations.size(0)
     if F != 1:
         raise ValueError("kv_chunk_shard: KV-chunk sharding is defined for single-turn caches")
@@ -63,9 +96,12 @@ def kv_chunk_shard(case: PagedCase, rank: int, world: int) -> PagedCase:
     loc = case.locations.to(torch.int64) - a
     loc = torch.clamp(loc, min=-1).to(torch.int32)
     bt = case.block_tables[:, a // BS: max(a // BS + 1, -(-b // BS))].contiguous()
+    kc, vc = case.k_cache, case.v_cache
+    if local_pages:
+        kc, vc, bt = compact_pages(kc, vc, bt)
     return PagedCase(queries=case.queries, locations=loc.contiguous(), cosines=case.cosines, sines=case.sines,
-                     fragment_lengths=torch.tensor([b - a], dtype=torch.int32, device=dev), k_cache=case.k_cache,
-                     v_cache=case.v_cache, block_tables=bt, scale=case.scale, turn_lens=case.turn_lens,
+                     fragment_lengths=torch.tensor([b - a], dtype=torch.int32, device=dev), k_cache=kc,
+                     v_cache=vc, block_tables=bt, scale=case.scale, turn_lens=case.turn_lens,
                      meta=dict(case.meta, chunk=(a, b)))
 
 
@@ -104,18 +140,35 @@ def packed_partials(out: torch.Tensor):
     return packed, packed[: rows * Ev].view(out.shape), packed[rows * Ev:].view(out.shape[:-1])
 
 
+def gather_buffer(packed: torch.Tensor, group=None) -> torch.Tensor:
+    """A receive buffer for allgather_merge_packed (allocated once and passed every step, so
+    the step allocates nothing and can be captured in a CUDA graph)."""
+    return torch.empty(dist.get_world_size(group) * packed.numel(), dtype=torch.float32, device=packed.device)
+
+
 def allgather_merge_packed(packed: torch.Tensor, out: torch.Tensor, group=None, merge: Optional[Callable] = None,
-                           lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                           lse_out: Optional[torch.Tensor] = None,
+                           gathered: Optional[torch.Tensor] = None) -> torch.Tensor:
     """allgather_merge with one all-gather: `packed` is this rank's buffer from
     packed_partials.  The default merge reads the gathered parts in place
     (dvattn_lse_merge_packed); an injected `merge` gets the same (part_out, part_lse, out,
-    lse_out) arguments as in allgather_merge."""
+    lse_out) arguments as in allgather_merge.  `gathered` (from gather_buffer) is the
+    receive buffer; without it one is allocated per call."""
     world = dist.get_world_size(group)
     Ev = out.size(-1)
     rows = out.numel() // Ev
     if packed.numel() != rows * (Ev + 1) or packed.dtype != torch.float32:
         raise ValueError("allgather_merge_packed: packed must be f32 with rows * (Ev + 1) elements")
-    g = torch.empty(world * packed.numel(), dtype=torch.float32, device=packed.device)
+    if packed.device != out.device:
+        raise ValueError("allgather_merge_packed: packed and out must be on the same device")
+    if gathered is None:
+        g = torch.empty(world * packed.numel(), dtype=torch.float32, device=packed.device)
+    else:
+        if gathered.numel() != world * packed.numel() or gathered.dtype != torch.float32 or \
+                gathered.device != packed.device or not gathered.is_contiguous():
+            raise ValueError("allgather_merge_packed: gathered must be contiguous f32 [world * packed.numel()] "
+                             "on packed's device")
+        g = gathered
     dist.all_gather_into_tensor(g, packed.contiguous().reshape(-1), group=group)
     g = g.view(world, rows * (Ev + 1))
     if merge is None:

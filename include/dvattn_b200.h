@@ -231,6 +231,20 @@ int dvattn_paged_sdpa_phase(const dvattn_paged_args* args, void* workspace, size
 size_t dvattn_paged_sdpa_noalloc_max_workspace(void);
 int dvattn_paged_sdpa_noalloc(const dvattn_paged_args* args, dvattn_stream_t stream);
 
+/*
+ * Error word of the last attention call that used `workspace` (dvattn_paged_sdpa,
+ * dvattn_varlen_paged_sdpa, dvattn_sdpa and their *_rope / *_phase forms), or, with
+ * workspace == NULL, of the last dvattn_paged_sdpa_noalloc call on the current device.
+ * Waits for `stream` (call it after the attention call, before the next call on the same
+ * workspace).  *error_word == 0: the call completed.  Nonzero: a bounded wait inside a
+ * kernel gave up (~2 s; bit 1 loader, bit 2 / 8 compute warps, bit 4 bad shared-memory
+ * alignment) and that call's outputs are invalid; the paged decode writes NaN to all of
+ * them, the tensor-core prefill to the rows of the items that gave up.  The reference
+ * reports kernel failures as a RuntimeError from C10_CUDA_CHECK (src/binding.cu:200,
+ * src/cuda_check.cuh:16-29); its kernels have no waits that can give up.
+ */
+int dvattn_workspace_status(const void* workspace, dvattn_stream_t stream, int* error_word);
+
 /* Workspace bytes of dvattn_varlen_paged_sdpa (see dvattn_paged_sdpa_workspace_size). */
 size_t dvattn_varlen_paged_sdpa_workspace_size(const dvattn_varlen_args* args);
 

@@ -278,7 +278,12 @@ def lse_merge(part_out: torch.Tensor, part_lse: torch.Tensor):
 # per-turn fragments and call sdpa_pt, the way a caller of the reference's eager path
 # would.  Used to pin the fast restatement above.
 # ---------------------------------------------------------------------------------
-def paged_via_sdpa_pt(scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables):
+def paged_via_sdpa_pt(scale, locations, queries, cosines, sines, fragment_lengths, k_cache, v_cache, block_tables,
+                      trim: bool = False):
+    """trim=True cuts each turn's fragment after the last key any row of the batch can see
+    (the keys cut are masked for every row, so the result is the same); with one sequence
+    per call this is the sequence's own visible length, as a caller with per-sequence
+    fragments would pass them."""
     loc = locations.cpu()
     L = fragment_lengths.cpu().numpy().astype(np.int64)
     bt = block_tables.cpu().numpy()
@@ -290,8 +295,9 @@ def paged_via_sdpa_pt(scale, locations, queries, cosines, sines, fragment_length
     vis_max = np.maximum(0, np.minimum(L[:, None], loc.numpy().max(axis=2) + 1))  # [F, W]
     keys, values = [], []
     for f in range(F):
-        Kf = torch.zeros(W, Hkv, int(L[f]), E, dtype=k_cache.dtype)
-        Vf = torch.zeros(W, Hkv, int(L[f]), v_cache.size(3), dtype=v_cache.dtype)
+        Lf = int(vis_max[f].max()) if (trim and W) else int(L[f])
+        Kf = torch.zeros(W, Hkv, Lf, E, dtype=k_cache.dtype)
+        Vf = torch.zeros(W, Hkv, Lf, v_cache.size(3), dtype=v_cache.dtype)
         for w in range(W):
             n = int(vis_max[f, w])
             K, V = gather_turn(k_cache.cpu(), v_cache.cpu(), bt[w], int(off[f]), n, BS, NB)

@@ -32,7 +32,8 @@ sys.path.insert(0, HERE)
 from dvattn_b200 import workloads as wl  # noqa: E402  (generators only; no native code)
 import fixtures  # noqa: E402
 
-REF = os.environ.get("DVATTN_REFERENCE", "/root/reference")
+# the reference checkout: DVATTN_REFERENCE, else a directory named "reference" beside the repo
+REF = os.environ.get("DVATTN_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def load_reference():

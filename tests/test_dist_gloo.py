@@ -155,3 +155,44 @@ def test_kv_chunk_bounds_are_page_aligned_and_cover():
         assert cb[0][0] == 0 and cb[-1][1] == total
         for (a, b), (c, d) in zip(cb, cb[1:]):
             assert b == c and a % bs == 0
+
+
+def _kv_shard_local_pages(rank, world):
+    c = _long_context_case()
+    sh = ddist.kv_chunk_shard(c, rank, world, local_pages=True)
+    # the rank keeps only its chunk's pages
+    assert sh.k_cache.size(0) <= sh.block_tables.numel() < c.k_cache.size(0)
+    o32, lse = O.paged_sdpa_f32(sh.scale, sh.locations, sh.queries, sh.cosines, sh.sines, sh.fragment_lengths,
+                                sh.k_cache, sh.v_cache, sh.block_tables)
+    packed, po, pl = ddist.packed_partials(o32)
+    po.copy_(o32)
+    pl.copy_(lse)
+    gathered = ddist.gather_buffer(packed)
+    out = torch.empty_like(o32)
+    with pytest.raises(ValueError):
+        ddist.allgather_merge_packed(packed, out, merge=_oracle_merge, gathered=gathered[1:])
+    ddist.allgather_merge_packed(packed, out, merge=_oracle_merge, gathered=gathered)
+    ref, _ = O.paged_sdpa_f32(c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths,
+                              c.k_cache, c.v_cache, c.block_tables)
+    torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-6)
+
+
+def test_kv_chunk_local_pages_and_gather_buffer_world2():
+    """Each rank holds only its chunk's pages; the preallocated receive buffer is used."""
+    res = _run(_kv_shard_local_pages)
+    assert all(v == "ok" for v in res.values()), res
+
+
+def test_shard_batch_matches_the_whole_batch():
+    """A rank's sequences with a pool of only their pages give the rows of the whole batch."""
+    c = wl.make_paged(wl.config2_lengths(2, 6), Hq=16, Hkv=2, E=64, R=32, BS=16, dtype=torch.float32, seed=7)
+    ref, rlse = O.paged_sdpa_f32(c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths,
+                                 c.k_cache, c.v_cache, c.block_tables)
+    for seqs in ([0, 3], [5], [1, 2, 4]):
+        sub = ddist.shard_batch(c, seqs)
+        used = np.unique(c.block_tables[seqs].numpy())
+        assert sub.k_cache.size(0) == int(((used >= 0) & (used < c.k_cache.size(0))).sum())
+        out, lse = O.paged_sdpa_f32(sub.scale, sub.locations, sub.queries, sub.cosines, sub.sines,
+                                    sub.fragment_lengths, sub.k_cache, sub.v_cache, sub.block_tables)
+        torch.testing.assert_close(out, ref[seqs], rtol=0, atol=0)
+        torch.testing.assert_close(lse, rlse[seqs], rtol=0, atol=0)

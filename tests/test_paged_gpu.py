@@ -197,7 +197,7 @@ def test_chained_call_reads_previous_output():
         assert torch.equal(out2, args3[0])
 
 
-def test_torch_op_on_side_stream_and_second_device_index():
+def test_torch_op_on_side_stream():
     import dvattn_b200
     c = wl.make_paged([[300, 45], [17, 900]], Hq=32, Hkv=2, E=128, R=32, BS=16, dtype=torch.bfloat16, seed=1).to(DEV)
     ref = c.new_out()
