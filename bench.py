@@ -137,15 +137,17 @@ def traffic_from_profiles(workload: str):
     return None
 
 
-def pipelined_e2e(host_in, out_like, launch, steps, warmup, world):
+def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 4):
     """End-to-end step time through a public API with host inputs and a host result, run
-    the way a serving loop runs it: each step's inputs (pinned host tensors, packed into
+    the way a serving loop runs it: every step's inputs (pinned host tensors, packed into
     one buffer) go to the device in ONE copy on an H2D stream, the op runs on the compute
-    stream, and its output comes back to pinned host memory on a D2H stream; input and
-    output buffers are double-buffered, so step i's copies overlap the op of step i-1, and
-    the K steps are captured once in a CUDA graph and replayed (no per-call host overhead),
-    falling back to eager issue if capture fails.  Every step's H2D and D2H copy is inside
-    the timed region.  `launch(dev_inputs, out, i)` enqueues the op on the current stream.
+    stream, and every step's output comes back to pinned host memory on a D2H stream right
+    after its op.  The H2D copies are issued in groups of `group` steps, one group ahead of
+    the compute, and the compute stream waits once per group (a wait in front of a kernel
+    costs it the programmatic overlap with the kernel before it, so the waits are batched);
+    device buffers form a ring of whole groups; the K steps are captured once in a CUDA
+    graph and replayed.  Every step's H2D and D2H copy is inside the timed region.
+    `launch(dev_inputs, out, i)` enqueues the op on the current stream.
     Returns (ms per step, H2D bytes, D2H bytes per step, mode)."""
     dev = out_like.device
     sizes = [t.numel() * t.element_size() for t in host_in]
@@ -156,42 +158,58 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world):
     host_flat = torch.empty(n, dtype=torch.uint8, pin_memory=True)
     for t, o, b in zip(host_in, offs, sizes):
         host_flat[o:o + b].copy_(t.contiguous().reshape(-1).view(torch.uint8))
-    dev_flat = [torch.empty(n, dtype=torch.uint8, device=dev) for _ in range(2)]
+    out_b = out_like.numel() * out_like.element_size()
+    # device buffers: a ring of R steps (a multiple of the group, at least two groups), all
+    # K steps when they fit in ~1 GB
+    fit = max(1, (1 << 30) // (n + out_b))
+    R = max(2 * group, min(steps + (-steps) % group, fit // group * group))
+    dev_flat = torch.empty((R, n), dtype=torch.uint8, device=dev)
     views = [[dev_flat[k][o:o + b].view(t.dtype).view(t.shape) for t, o, b in zip(host_in, offs, sizes)]
-             for k in range(2)]
-    outs = [torch.empty_like(out_like) for _ in range(2)]
+             for k in range(R)]
+    outs = [torch.empty_like(out_like) for _ in range(R)]
     host_out = [torch.empty(out_like.shape, dtype=out_like.dtype, pin_memory=True) for _ in range(2)]
     h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    ev_in = [torch.cuda.Event() for _ in range(2)]
-    ev_comp = [torch.cuda.Event() for _ in range(2)]
-    ev_d2h = [torch.cuda.Event() for _ in range(2)]
 
     def run(nsteps):
         main = torch.cuda.current_stream()
         h2d_s.wait_stream(main)
         d2h_s.wait_stream(main)
-        for i in range(nsteps):
-            k = i & 1
+        ngroups = -(-nsteps // group)
+        ev_in, ev_op, ev_d2h = [None] * ngroups, [None] * nsteps, [None] * nsteps
+
+        def issue_h2d(g):
             with torch.cuda.stream(h2d_s):
-                if i >= 2:
-                    h2d_s.wait_event(ev_comp[k])  # the op of step i-2 has read dev_flat[k]
-                dev_flat[k].copy_(host_flat, non_blocking=True)
-                ev_in[k].record(h2d_s)
-            main.wait_event(ev_in[k])
-            if i >= 2:
-                main.wait_event(ev_d2h[k])  # step i-2's result has been read back from outs[k]
-            launch(views[k], outs[k], i)
-            ev_comp[k].record(main)
-            with torch.cuda.stream(d2h_s):
-                d2h_s.wait_event(ev_comp[k])
-                host_out[k].copy_(outs[k], non_blocking=True)
-                ev_d2h[k].record(d2h_s)
+                reuse = g * group + group - 1 - R  # last op that read these input buffers
+                if reuse >= 0:
+                    h2d_s.wait_event(ev_op[reuse])
+                for i in range(g * group, min(g * group + group, nsteps)):
+                    dev_flat[i % R].copy_(host_flat, non_blocking=True)
+                ev_in[g] = torch.cuda.Event()
+                ev_in[g].record(h2d_s)
+
+        issue_h2d(0)
+        for g in range(ngroups):
+            if g + 1 < ngroups:
+                issue_h2d(g + 1)  # one group ahead of the compute
+            main.wait_event(ev_in[g])
+            reuse = g * group + group - 1 - R  # last D2H that read these output buffers
+            if reuse >= 0:
+                main.wait_event(ev_d2h[reuse])
+            for i in range(g * group, min(g * group + group, nsteps)):
+                launch(views[i % R], outs[i % R], i)
+                ev_op[i] = torch.cuda.Event()
+                ev_op[i].record(main)
+                with torch.cuda.stream(d2h_s):
+                    d2h_s.wait_event(ev_op[i])
+                    host_out[i % 2].copy_(outs[i % R], non_blocking=True)
+                    ev_d2h[i] = torch.cuda.Event()
+                    ev_d2h[i].record(d2h_s)
         main.wait_stream(h2d_s)
         main.wait_stream(d2h_s)
 
     run(warmup)
     torch.cuda.synchronize()
-    mode = "cuda-graph"
+    mode = f"cuda-graph, H2D in groups of {group} steps"
     graph = None
     try:
         graph = torch.cuda.CUDAGraph()
@@ -200,19 +218,13 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world):
         graph.replay()
         torch.cuda.synchronize()
     except Exception:  # capture unsupported for this op: issue eagerly
-        graph, mode = None, "eager"
+        graph, mode = None, f"eager, H2D in groups of {group} steps"
         torch.cuda.synchronize()
     barrier(world)
     main = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(main)
-    if graph is not None:
-        graph.replay()
-    else:
-        run(steps)
-    e1.record(main)
-    torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    per_rep = timed_reps((lambda k: graph.replay()) if graph is not None else (lambda k: run(steps)), 1, world,
+                         main, min_reps=10, min_s=0.3)
+    ms = statistics.median(per_rep) / steps
     return ms, sum(sizes), host_out[0].numel() * host_out[0].element_size(), mode
 
 
@@ -502,10 +514,20 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     if sampler:
         sampler.begin()
-    # K steps timed as one rep; reps repeated (>= 25, ~1 s of work) for the clock record
-    # and the spread; value = the median rep
-    per_rep = timed_reps(lambda i: calls[i % 3](), args.steps, world, stream)
+    # K steps captured once in a CUDA graph (as a serving loop issues a decode step) and
+    # replayed; each replay is one rep of K steps, repeated (>= 25, ~1 s of work) for the
+    # clock record and the spread; value = the median rep
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            calls[i % 3]()
+    graph.replay()
+    torch.cuda.synchronize()
+    per_rep = timed_reps(lambda k: graph.replay(), 1, world, stream)
     t_ms = statistics.median(per_rep) / args.steps
+    # the same K calls issued eagerly from the host (no graph), for comparison
+    per_rep_eager = timed_reps(lambda i: calls[i % 3](), args.steps, world, stream, min_reps=10, min_s=0.2)
+    t_eager = statistics.median(per_rep_eager) / args.steps
 
     # ---- attention kernel alone (roofline), same stream, events between phases ----
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -572,8 +594,9 @@ def run_ours(args, world, rank, local):
             "data": "synthetic (seeded N(0,1) q/k/v, seeded lengths/turns/page permutation)",
             "config": paged_config(args.workload, nbytes, world,
                                    (case.k_cache.numel() + case.v_cache.numel()) * case.k_cache.element_size()),
-            "timing": dict(spread(per_rep, args.steps), value_from="median rep; each rep = K steps between CUDA "
-                           "events after a barrier and a synchronise, max over ranks"),
+            "timing": dict(spread(per_rep, args.steps), value_from="median rep; each rep = one CUDA-graph replay "
+                           "of the K C-ABI calls between CUDA events after a barrier and a synchronise, max over "
+                           "ranks", us_per_step_eager=round(t_eager * 1e3, 2)),
             "roofline": {"bound": "hbm", "kernel": "decode_row_kernel" if case.dtype != torch.float32 else
                          "decode_f32_kernel", "achieved": round(achieved, 2), "peak": hbm_peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
@@ -585,7 +608,8 @@ def run_ours(args, world, rank, local):
                          "frac_back_to_back": round(nbytes / (kb_ms * 1e-3) / 1e9 / hbm_peak, 4)},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_layer_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_paged_sdpa", "issue": e2e_mode,
-                    "copies": "per step one packed H2D of its inputs and one D2H of its output on copy streams, double-buffered (overlapping the neighbouring steps' ops)"},
+                    "copies": "per step one packed H2D of its inputs (issued in groups of 4 steps ahead of the "
+                              "compute) and one D2H of its output right after its op, on copy streams"},
             "gpu_launches": launches_per_step * args.steps * len(per_rep),
             "gpu_launches_per_step": launches_per_step,
             "clocks": clocks,
@@ -1016,14 +1040,21 @@ def graph_step_ms(fns, steps: int, world: int, min_reps: int = 25, min_s: float 
     return [x / steps for x in per_rep]
 
 
-def paged_calls(case, n_pools: int, **kw):
+def kv_pools(case, n_pools: int):
+    """The case's KV pool and n_pools - 1 random copies of it."""
+    pools = [(case.k_cache, case.v_cache)]
+    for _ in range(n_pools - 1):
+        pools.append((torch.randn_like(case.k_cache, dtype=torch.float32).to(case.dtype),
+                      torch.randn_like(case.v_cache, dtype=torch.float32).to(case.dtype)))
+    return pools
+
+
+def paged_calls(case, n_pools: int, out=None, workspace=None, **kw):
     """PagedCall objects over `n_pools` copies of the case's KV pool (one shared workspace)."""
     from dvattn_b200 import capi
-    out = case.new_out()
-    calls, ws = [], None
-    for i in range(n_pools):
-        kc = case.k_cache if i == 0 else torch.randn_like(case.k_cache, dtype=torch.float32).to(case.dtype)
-        vc = case.v_cache if i == 0 else torch.randn_like(case.v_cache, dtype=torch.float32).to(case.dtype)
+    out = case.new_out() if out is None else out
+    calls, ws = [], workspace
+    for kc, vc in kv_pools(case, n_pools):
         c = capi.PagedCall(out, case.scale, case.locations, case.queries, case.cosines, case.sines,
                            case.fragment_lengths, kc, vc, case.block_tables, workspace=ws, **kw)
         ws = c.workspace
@@ -1079,53 +1110,84 @@ def long3_scaling(world: int, rank: int, dev: str, steps: int) -> dict:
     del full
     torch.cuda.empty_cache()
     out = sh.new_out()
-    packed, o32, lse = ddist.packed_partials(out)
-    gathered = ddist.gather_buffer(packed)
     merged = torch.empty_like(out)
     pb = (sh.k_cache.numel() + sh.v_cache.numel()) * sh.k_cache.element_size()
-    calls, _ = paged_calls(sh, pool_copies(pb), lse=lse, out_f32=o32)
-    import torch.distributed as tdist
+    n_pools = pool_copies(pb)
+    steps_g = steps + (steps & 1)  # the peer exchange alternates two slots: an even count per replay
     Ev = out.size(-1)
     rows = out.numel() // Ev
+    import torch.distributed as tdist
 
-    def step_fn(c):
+    # (a) peer-memory exchange: attention writes its partial into this rank's exchange
+    # region; one kernel signals, waits for every rank and merges from the peers' memory
+    ex = ddist.PeerExchange(out)
+    pools = kv_pools(sh, n_pools)
+    pcalls, ws = [], None
+    for i in range(2 * n_pools):
+        o32, lse = ex.outputs(i % 2)
+        kc, vc = pools[i % n_pools]
+        c = capi.PagedCall(out, sh.scale, sh.locations, sh.queries, sh.cosines, sh.sines, sh.fragment_lengths,
+                           kc, vc, sh.block_tables, lse=lse, out_f32=o32, workspace=ws)
+        ws = c.workspace
+        pcalls.append(c)
+
+    def peer_step(i):
+        def f():
+            pcalls[i]()
+            ex.merge(i % 2, merged)
+        return f
+
+    def peer_merge(i):
+        return lambda: ex.merge(i % 2, merged)
+
+    # (b) NCCL: one all-gather of the packed partials + the packed merge
+    packed, o32n, lsen = ddist.packed_partials(out)
+    gathered = ddist.gather_buffer(packed)
+    ncalls = [capi.PagedCall(out, sh.scale, sh.locations, sh.queries, sh.cosines, sh.sines, sh.fragment_lengths,
+                             kc, vc, sh.block_tables, lse=lsen, out_f32=o32n, workspace=ws) for kc, vc in pools]
+
+    def nccl_step(c):
         def f():
             c()
             ddist.allgather_merge_packed(packed, merged, gathered=gathered)
         return f
 
-    def attend_fn(c):
-        return lambda: c()
-
     def exchange():
         tdist.all_gather_into_tensor(gathered, packed)
 
-    def merge():
+    def nccl_merge():
         capi.lse_merge_packed(gathered.view(world, rows * (Ev + 1)), merged)
 
+    med = lambda fns: statistics.median(graph_step_ms(fns, steps_g, world))  # noqa: E731
+    tn = med([peer_step(i) for i in range(2 * n_pools)])
+    t_att = med([(lambda c=c: c()) for c in pcalls])
+    t_pm = med([peer_merge(i) for i in range(2)])
+    assert ex.status() == 0, "peer exchange: a wait ran out"
     mode = "cuda-graph"
     try:
-        tn = statistics.median(graph_step_ms([step_fn(c) for c in calls], steps, world))
-        t_att = statistics.median(graph_step_ms([attend_fn(c) for c in calls], steps, world))
-        t_ex = statistics.median(graph_step_ms([exchange], steps, world))
-        t_mg = statistics.median(graph_step_ms([merge], steps, world))
+        tn_nccl = med([nccl_step(c) for c in ncalls])
+        t_ex = med([exchange])
+        t_mg = med([nccl_merge])
     except Exception as e:  # a collective that cannot be captured: time eagerly
         mode = "eager (%s)" % str(e).splitlines()[0][:80]
         torch.cuda.synchronize()
         st = torch.cuda.current_stream()
-        fs = [step_fn(c) for c in calls]
-        tn = statistics.median(timed_reps(lambda k: fs[k % len(fs)](), steps, world, st)) / steps
-        fa = [attend_fn(c) for c in calls]
-        t_att = statistics.median(timed_reps(lambda k: fa[k % len(fa)](), steps, world, st)) / steps
+        fs = [nccl_step(c) for c in ncalls]
+        tn_nccl = statistics.median(timed_reps(lambda k: fs[k % len(fs)](), steps, world, st)) / steps
         t_ex = statistics.median(timed_reps(lambda k: exchange(), steps, world, st)) / steps
-        t_mg = statistics.median(timed_reps(lambda k: merge(), steps, world, st)) / steps
+        t_mg = statistics.median(timed_reps(lambda k: nccl_merge(), steps, world, st)) / steps
+    ex.close()
     return {"us_per_step": round(tn * 1e3, 2), "us_per_step_1gpu": round(t1 * 1e3, 2),
             "gbs": round(nbytes / (tn * 1e-3) / 1e9, 1), "efficiency_vs_1gpu": round(t1 / (world * tn), 4),
-            "attention_us": round(t_att * 1e3, 2), "exchange_us": round(t_ex * 1e3, 2),
-            "merge_us": round(t_mg * 1e3, 2), "exchange_bytes_per_rank": packed.numel() * 4,
-            "parallelism": f"kv-chunk x{world}, local pages only", "issue": mode,
-            "timing": "per step: attention + NCCL all_gather_into_tensor + dvattn_lse_merge_packed; median of "
-                      "reps, max over ranks; the parts timed alone the same way"}
+            "attention_us": round(t_att * 1e3, 2), "peer_merge_us": round(t_pm * 1e3, 2),
+            "exchange": "peer memory: dvattn_lse_merge_peers (signal, bounded wait, merge reading the peers' "
+                        "partials over NVLink), one kernel after the attention",
+            "nccl": {"us_per_step": round(tn_nccl * 1e3, 2), "efficiency_vs_1gpu": round(t1 / (world * tn_nccl), 4),
+                     "all_gather_us": round(t_ex * 1e3, 2), "merge_us": round(t_mg * 1e3, 2), "issue": mode},
+            "exchange_bytes_per_rank": rows * (Ev + 1) * 4,
+            "parallelism": f"kv-chunk x{world}, local pages only",
+            "timing": "per step: attention + exchange + merge, CUDA-graph replay of K steps, median of reps, "
+                      "max over ranks; the parts timed alone the same way"}
 
 
 def run_long3(args, world, rank, local):

@@ -22,7 +22,7 @@ BUILD = os.path.join(ROOT, "_build")
 CAPI_SO = os.path.join(HERE, "libdvattn_b200.so")
 TORCH_SO = os.path.join(HERE, "dvatt.abi3.so")
 
-CU_SOURCES = ["decode.cu", "rope.cu", "merge.cu", "capi.cu", "noalloc.cu", "prefill.cu", "append.cu", "views.cu",
+CU_SOURCES = ["decode.cu", "rope.cu", "merge.cu", "capi.cu", "noalloc.cu", "peer.cu", "prefill.cu", "append.cu", "views.cu",
               "rope_tables.cu"]
 HEADERS = ["common.cuh", "schedule.cuh", "decode.cuh", "tma_host.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

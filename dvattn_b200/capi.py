@@ -50,6 +50,13 @@ EXPORTS = [
     "dvattn_varlen_rope",
     "dvattn_lse_merge",
     "dvattn_lse_merge_packed",
+    "dvattn_peer_region_bytes",
+    "dvattn_peer_slot_offset",
+    "dvattn_peer_region_alloc",
+    "dvattn_peer_region_open",
+    "dvattn_peer_region_close",
+    "dvattn_peer_region_free",
+    "dvattn_lse_merge_peers",
     "dvattn_sdpa_workspace_size",
     "dvattn_sdpa",
     "dvattn_paged_append",
@@ -150,6 +157,20 @@ def lib() -> ctypes.CDLL:
         L.dvattn_lse_merge.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp, _vp]
         L.dvattn_lse_merge_packed.restype = _i
         L.dvattn_lse_merge_packed.argtypes = [_i, _i, ctypes.c_longlong, _i, _vp, _vp, _vp, _vp]
+        L.dvattn_peer_region_bytes.restype = ctypes.c_size_t
+        L.dvattn_peer_region_bytes.argtypes = [ctypes.c_longlong, _i]
+        L.dvattn_peer_slot_offset.restype = ctypes.c_size_t
+        L.dvattn_peer_slot_offset.argtypes = [ctypes.c_longlong, _i, _i]
+        L.dvattn_peer_region_alloc.restype = _i
+        L.dvattn_peer_region_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]
+        L.dvattn_peer_region_open.restype = _i
+        L.dvattn_peer_region_open.argtypes = [_vp, ctypes.POINTER(_vp)]
+        L.dvattn_peer_region_close.restype = _i
+        L.dvattn_peer_region_close.argtypes = [_vp]
+        L.dvattn_peer_region_free.restype = _i
+        L.dvattn_peer_region_free.argtypes = [_vp]
+        L.dvattn_lse_merge_peers.restype = _i
+        L.dvattn_lse_merge_peers.argtypes = [_i, _i, _i, _i, ctypes.c_longlong, _i, ctypes.POINTER(_vp), _vp, _vp, _vp]
         L.dvattn_paged_append.restype = _i
         L.dvattn_paged_append.argtypes = [ctypes.POINTER(AppendArgs), _vp]
         L.dvattn_paged_sdpa_rope_workspace_size.restype = ctypes.c_size_t
@@ -354,6 +375,82 @@ def lse_merge_packed(packed, out, lse_out=None):
                                        _ptr(lse_out), _stream(None))
     if st != DVATTN_OK:
         raise DvattnError(st, "dvattn_lse_merge_packed")
+    return out
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ of device memory this library allocated, so that torch can
+    view it without a copy (the view does not own the memory)."""
+
+    def __init__(self, ptr: int, shape, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3}
+
+
+def device_view(ptr: int, numel: int, device) -> torch.Tensor:
+    """A float32 torch tensor over `numel` floats of device memory at `ptr` (no copy)."""
+    return torch.as_tensor(_DeviceArray(ptr, (numel,)), device=device)
+
+
+class PeerRegion:
+    """One rank's exchange region for dvattn_lse_merge_peers (allocated by the library with
+    cudaMalloc; its CUDA IPC handle lets the other ranks map it)."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, rows: int, Ev: int, device):
+        self.rows, self.Ev = int(rows), int(Ev)
+        self.nbytes = lib().dvattn_peer_region_bytes(self.rows, self.Ev)
+        if self.nbytes == 0:
+            raise DvattnError(DVATTN_ERR_INVALID_ARGUMENT, "dvattn_peer_region_bytes")
+        self.device = torch.device(device)
+        ptr = _vp()
+        self.handle = (ctypes.c_char * self.HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            st = lib().dvattn_peer_region_alloc(self.nbytes, ctypes.byref(ptr), self.handle)
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_peer_region_alloc")
+        self.ptr = ptr.value
+
+    def slot(self, s: int):
+        """(packed f32 [rows * (Ev + 1)], out_f32 view [rows * Ev], lse view [rows]) of slot s."""
+        off = lib().dvattn_peer_slot_offset(self.rows, self.Ev, s)
+        packed = device_view(self.ptr + off, self.rows * (self.Ev + 1), self.device)
+        return packed, packed[: self.rows * self.Ev], packed[self.rows * self.Ev:]
+
+    def status(self) -> int:
+        word = _i(0)
+        st = lib().dvattn_workspace_status(self.ptr, _stream(None), ctypes.byref(word))
+        if st != DVATTN_OK:
+            raise DvattnError(st, "dvattn_workspace_status")
+        return word.value
+
+    def free(self):
+        if self.ptr:
+            with torch.cuda.device(self.device):
+                lib().dvattn_peer_region_free(self.ptr)
+            self.ptr = None
+
+
+def open_peer_region(handle: bytes, device) -> int:
+    """Map another rank's region (its IPC handle) into this process; returns the pointer."""
+    ptr = _vp()
+    buf = (ctypes.c_char * PeerRegion.HANDLE_BYTES).from_buffer_copy(handle)
+    with torch.cuda.device(torch.device(device)):
+        st = lib().dvattn_peer_region_open(buf, ctypes.byref(ptr))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_peer_region_open")
+    return ptr.value
+
+
+def lse_merge_peers(regions, rank: int, slot: int, rows: int, Ev: int, out, lse_out=None):
+    """dvattn_lse_merge_peers on the current stream; regions = device pointers of every
+    rank's region as mapped in this process."""
+    arr = (_vp * len(regions))(*regions)
+    st = lib().dvattn_lse_merge_peers(_DTYPE.get(out.dtype, -1), len(regions), rank, slot, rows, Ev, arr,
+                                      out.data_ptr(), _ptr(lse_out), _stream(None))
+    if st != DVATTN_OK:
+        raise DvattnError(st, "dvattn_lse_merge_peers")
     return out
 
 

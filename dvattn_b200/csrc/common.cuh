@@ -113,6 +113,17 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk, int row_bytes) {
     return static_cast<uint32_t>(row * row_bytes + ((chunk ^ (row & 7)) << 4));
 }
 
+// Four consecutive output values of type T in one 8-byte (16-bit T) or 16-byte store.
+template <class T> __device__ __forceinline__ void store_quad(T* dst, float a, float b, float c, float d) {
+    uint2 pk;
+    pk.x = Elem<T>::pack2(a, b);
+    pk.y = Elem<T>::pack2(c, d);
+    *reinterpret_cast<uint2*>(dst) = pk;
+}
+template <> __device__ __forceinline__ void store_quad<float>(float* dst, float a, float b, float c, float d) {
+    *reinterpret_cast<float4*>(dst) = make_float4(a, b, c, d);
+}
+
 // ----------------------------------------------------------------------------------
 // mbarriers, TMA (non-multicast tiled loads), named barriers, proxy fences
 // ----------------------------------------------------------------------------------

@@ -140,6 +140,67 @@ def packed_partials(out: torch.Tensor):
     return packed, packed[: rows * Ev].view(out.shape), packed[rows * Ev:].view(out.shape[:-1])
 
 
+class PeerExchange:
+    """KV-sharded partials exchanged over peer memory: every rank holds one exchange region
+    (two slots of packed f32 outputs + LSEs), the regions are mapped into every rank through
+    CUDA IPC handles (exchanged once with all_gather_object), and one kernel per step
+    signals, waits for every rank (bounded) and merges the partials read from the peers'
+    memory (dvattn_lse_merge_peers).  Replaces the all-gather + merge pair of
+    allgather_merge_packed; the step allocates nothing and can be captured in a CUDA graph.
+
+    Use: o32, lse = ex.outputs(slot) as the attention call's out_f32 / lse_out, then
+    ex.merge(slot, out); consecutive steps alternate slot 0 / 1."""
+
+    def __init__(self, out: torch.Tensor, group=None):
+        from . import capi
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("PeerExchange: at most 8 ranks")
+        self.shape = tuple(out.shape)
+        self.Ev = out.size(-1)
+        self.rows = out.numel() // self.Ev
+        self.region = capi.PeerRegion(self.rows, self.Ev, out.device)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(self.region.handle), group=group)
+        self.opened = []
+        ptrs = []
+        for j, h in enumerate(handles):
+            if j == self.rank:
+                ptrs.append(self.region.ptr)
+            else:
+                p = capi.open_peer_region(h, out.device)
+                self.opened.append(p)
+                ptrs.append(p)
+        self.regions = ptrs
+        self._slots = [self.region.slot(s) for s in (0, 1)]
+
+    def outputs(self, slot: int):
+        """(out_f32 [out.shape] f32, lse [out.shape[:-1]] f32) views of this rank's slot."""
+        _, o32, lse = self._slots[slot]
+        return o32.view(self.shape), lse.view(self.shape[:-1])
+
+    def merge(self, slot: int, out: torch.Tensor, lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        from . import capi
+        return capi.lse_merge_peers(self.regions, self.rank, slot, self.rows, self.Ev, out, lse_out)
+
+    def status(self) -> int:
+        """Error word of this rank's region: nonzero when a wait for another rank ran out."""
+        return self.region.status()
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (after every rank is done)."""
+        from . import capi
+        torch.cuda.synchronize(self.region.device)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            capi.lib().dvattn_peer_region_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)
+        self.region.free()
+
+
 def gather_buffer(packed: torch.Tensor, group=None) -> torch.Tensor:
     """A receive buffer for allgather_merge_packed (allocated once and passed every step, so
     the step allocates nothing and can be captured in a CUDA graph)."""

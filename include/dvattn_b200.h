@@ -344,6 +344,34 @@ int dvattn_lse_merge(int dtype, int num_parts, long long rows, int Ev, const flo
 int dvattn_lse_merge_packed(int dtype, int num_parts, long long rows, int Ev, const float* packed,
                             void* out, float* lse_out, dvattn_stream_t stream);
 
+/*
+ * KV-sharded partials exchanged over peer memory (NVLink) instead of a collective: one
+ * kernel per rank signals that its partial is complete, waits (bounded, ~2 s) for every
+ * rank's signal, and merges all ranks' partials read straight from their memory.  No
+ * reference counterpart (the reference runs on one GPU); the merge arithmetic is its
+ * split-KV reduce (src/kernels/paged_kernel_v21.cuh:347-363).
+ *
+ * Each rank allocates one exchange region of dvattn_peer_region_bytes(rows, Ev)
+ * (dvattn_peer_region_alloc: cudaMalloc, zeroed, plus its 64-byte CUDA IPC handle), sends
+ * the handle to the other ranks, and maps theirs (dvattn_peer_region_open).  A region has
+ * two slots; slot s holds a rank's packed partial at dvattn_peer_slot_offset(rows, Ev, s):
+ * [rows][Ev] f32 outputs, then [rows] f32 natural-log LSEs (pass them as the attention
+ * call's out_f32 / lse_out).  Consecutive calls must alternate slots.
+ * dvattn_lse_merge_peers(dtype, world, rank, slot, rows, Ev, regions, out, lse_out,
+ * stream): regions[j] = rank j's region as mapped on this rank (regions[rank] = own);
+ * out [rows][Ev] T, optional lse_out [rows].  All ranks make the same sequence of calls.
+ * A wait that runs out sets the error word (dvattn_workspace_status(own region, ...))
+ * and writes NaN to this call's outputs.  world <= 8.
+ */
+size_t dvattn_peer_region_bytes(long long rows, int Ev);
+size_t dvattn_peer_slot_offset(long long rows, int Ev, int slot);
+int dvattn_peer_region_alloc(size_t bytes, void** region, void* ipc_handle);
+int dvattn_peer_region_open(const void* ipc_handle, void** region);
+int dvattn_peer_region_close(void* region);
+int dvattn_peer_region_free(void* region);
+int dvattn_lse_merge_peers(int dtype, int world, int rank, int slot, long long rows, int Ev, void* const* regions,
+                           void* out, float* lse_out, dvattn_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

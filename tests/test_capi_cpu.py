@@ -127,3 +127,20 @@ def test_unknown_dtype_raises():
                                              torch.empty(1, 1, 1, 64), torch.empty(1, 1, 1, 64),
                                              torch.ones(1, dtype=torch.int32), torch.empty(1, 16, 1, 128),
                                              torch.empty(1, 16, 1, 128), torch.zeros(1, 1, dtype=torch.int32))
+
+
+def test_peer_exchange_validation_without_gpu():
+    lib = capi.lib()
+    assert lib.dvattn_peer_region_bytes(512, 128) == 256 + 2 * ((512 * 129 * 4 + 255) // 256 * 256)
+    assert lib.dvattn_peer_region_bytes(512, 6) == 0  # Ev must be a multiple of 4
+    assert lib.dvattn_peer_slot_offset(512, 128, 0) == 256
+    assert lib.dvattn_peer_slot_offset(512, 128, 2) == 0
+    regions = (ctypes.c_void_p * 2)(None, None)
+    for world, rank, slot in ((0, 0, 0), (9, 0, 0), (2, 2, 0), (2, 0, 2)):
+        assert lib.dvattn_lse_merge_peers(capi.DVATTN_BFLOAT16, world, rank, slot, 16, 128, regions, 1, None,
+                                          None) == capi.DVATTN_ERR_INVALID_ARGUMENT
+    # null or misaligned region pointers are refused before any launch
+    assert lib.dvattn_lse_merge_peers(capi.DVATTN_BFLOAT16, 2, 0, 0, 16, 128, regions, 1, None,
+                                      None) == capi.DVATTN_ERR_INVALID_ARGUMENT
+    assert lib.dvattn_peer_region_alloc(16, None, None) == capi.DVATTN_ERR_INVALID_ARGUMENT
+    assert lib.dvattn_workspace_status(None, None, None) == capi.DVATTN_ERR_INVALID_ARGUMENT
