@@ -159,11 +159,9 @@ __device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, i
                      (((size_t)w * p.Hq + (row >> 4) * p.gqa + (g < p.gqa ? g : 0)) * p.S + s) * E + ch * 8;
         cp_async16_zfill(smem_u32(slot(row, ch)), q, g < p.gqa ? 16 : 0);
     }
-    if (sCS) {  // cos/sin rows staged in shared memory (else read per pair from L1/L2)
-        for (int k = tid; k < 2 * (hp >> 2); k += nth) {
-            const int half = k / (hp >> 2), jj = k - half * (hp >> 2);
-            cp_async16_zfill(smem_u32(sCS + half * hp + jj * 4), (half ? sr : cr) + jj * 4, 16);
-        }
+    for (int k = tid; k < 2 * (hp >> 2); k += nth) {
+        const int half = k / (hp >> 2), jj = k - half * (hp >> 2);
+        cp_async16_zfill(smem_u32(sCS + half * hp + jj * 4), (half ? sr : cr) + jj * 4, 16);
     }
     cp_async_commit();
     cp_async_wait<0>();
@@ -177,27 +175,10 @@ __device__ __forceinline__ void rotate_q_inplace(const PagedParams& p, int ws, i
         const T* x = reinterpret_cast<const T*>(&xv);
         const T* y = reinterpret_cast<const T*>(&yv);
         uint32_t lo[4], hi[4];
-        float cc[8], ss[8];
-        if (sCS) {
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                cc[u] = sCS[j * 8 + u];
-                ss[u] = sCS[hp + j * 8 + u];
-            }
-        } else {
-            const float4 c_lo = __ldg(reinterpret_cast<const float4*>(cr + j * 8));
-            const float4 c_hi = __ldg(reinterpret_cast<const float4*>(cr + j * 8) + 1);
-            const float4 s_lo = __ldg(reinterpret_cast<const float4*>(sr + j * 8));
-            const float4 s_hi = __ldg(reinterpret_cast<const float4*>(sr + j * 8) + 1);
-            cc[0] = c_lo.x; cc[1] = c_lo.y; cc[2] = c_lo.z; cc[3] = c_lo.w;
-            cc[4] = c_hi.x; cc[5] = c_hi.y; cc[6] = c_hi.z; cc[7] = c_hi.w;
-            ss[0] = s_lo.x; ss[1] = s_lo.y; ss[2] = s_lo.z; ss[3] = s_lo.w;
-            ss[4] = s_hi.x; ss[5] = s_hi.y; ss[6] = s_hi.z; ss[7] = s_hi.w;
-        }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float c0 = cc[2 * u], c1 = cc[2 * u + 1];
-            const float s0 = ss[2 * u], s1 = ss[2 * u + 1];
+            const float c0 = sCS[j * 8 + 2 * u], c1 = sCS[j * 8 + 2 * u + 1];
+            const float s0 = sCS[hp + j * 8 + 2 * u], s1 = sCS[hp + j * 8 + 2 * u + 1];
             const float x0 = Elem<T>::to_f(x[2 * u]), x1 = Elem<T>::to_f(x[2 * u + 1]);
             const float y0 = Elem<T>::to_f(y[2 * u]), y1 = Elem<T>::to_f(y[2 * u + 1]);
             lo[u] = Elem<T>::pack2(x0 * c0 - y0 * s0, x1 * c1 - y1 * s1);
@@ -936,18 +917,13 @@ struct RowCfg {
     // With q fragments held in registers (E <= 128) the rotation buffer is only used at a
     // turn change and the merge buffer only at a row's end, so the two share memory.
     static constexpr size_t OFF_O = QREG ? OFF_Q : OFF_Q + QBYTES;
-    // Stage descriptors, barriers and the abort flag follow the q / merge buffers; the
-    // cross-warp merge statistics (used only when several warps serve one KV head) and the
-    // cos/sin staging of the scalar rotation path come last, so a launch that needs neither
-    // can leave them out (SMEM_ONE_WARP_PER_HEAD).
-    static constexpr size_t OFF_DESC = QREG ? OFF_Q + (QBYTES > OBYTES ? QBYTES : OBYTES) : OFF_O + OBYTES;
+    static constexpr size_t OFF_ML = QREG ? OFF_Q + (QBYTES > OBYTES ? QBYTES : OBYTES) : OFF_O + OBYTES;
+    static constexpr size_t OFF_LSE = OFF_ML + (CW * 16 * 2 > E ? CW * 16 * 2 : E) * 4;
+    static constexpr size_t OFF_DESC = OFF_LSE + 2 * 16 * 4;
     static constexpr size_t OFF_BAR = OFF_DESC + STAGES * 32;
     static constexpr size_t OFF_FLAG = OFF_BAR + STAGES * 16;
-    static constexpr size_t SMEM_ONE_WARP_PER_HEAD = OFF_FLAG + 16;
-    static constexpr size_t OFF_ML = SMEM_ONE_WARP_PER_HEAD;
-    static constexpr size_t OFF_LSE = OFF_ML + (CW * 16 * 2 > E ? CW * 16 * 2 : E) * 4;
     static constexpr size_t OFF_CS = OFF_ML;  // cos/sin staging of a rotation aliases the merge stats
-    static constexpr size_t SMEM = OFF_LSE + 2 * 16 * 4;
+    static constexpr size_t SMEM = OFF_FLAG + 16;
 };
 
 // Tensor maps of up to kParamFrags contiguous fragments, passed by value to the row kernel
@@ -980,9 +956,6 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     const uint32_t bar_full = s0 + (uint32_t)C::OFF_BAR;
     const uint32_t bar_empty = bar_full + STAGES * 8;
     volatile int* sAbort = reinterpret_cast<volatile int*>(smem + C::OFF_FLAG);
-    // launched with SMEM_ONE_WARP_PER_HEAD (p.small_smem): nothing past OFF_FLAG exists, so
-    // the rotation reads cos/sin from L1/L2 instead of staging them at OFF_CS
-    float* sCS = p.small_smem ? nullptr : reinterpret_cast<float*>(smem + C::OFF_CS);
 
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int Hkv = p.Hkv;
@@ -1194,7 +1167,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         it0.align = TOKB;
         TileDesc d0;
         if (it0.next(p, d0)) {
-            rotate_q_inplace<T, E>(p, d0.ws, d0.f, Hkv, sQ, tid, CW * 32, sCS, 2);
+            rotate_q_inplace<T, E>(p, d0.ws, d0.f, Hkv, sQ, tid, CW * 32,
+                                                                           reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -1227,7 +1201,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         }
         if ((d.flags & 2) && i > 0) {
             named_bar_sync(2, CW * 32);
-            rotate_q_inplace<T, E>(p, d.ws, d.f, Hkv, sQ, tid, CW * 32, sCS, 2);
+            rotate_q_inplace<T, E>(p, d.ws, d.f, Hkv, sQ, tid, CW * 32,
+                                                                           reinterpret_cast<float*>(smem + C::OFF_CS), 2);
             named_bar_sync(2, CW * 32);
             if constexpr (C::QREG) {
 #pragma unroll
@@ -1328,7 +1303,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
 
         if (d.flags & 4) {
             // first global writes of this warp: after the previous grid has completed
-            if (p.fused && !p.exp_nowait) asm volatile("griddepcontrol.wait;" ::: "memory");
+            if (p.fused) asm volatile("griddepcontrol.wait;" ::: "memory");
             // ---- finish this row piece: per head, combine its wph warps ----
             float lt0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
             lt0 += __shfl_xor_sync(0xffffffffu, lt0, 2);
@@ -1748,125 +1723,6 @@ __device__ __forceinline__ void merge_segment(const PagedParams& p, int g_seg, c
     if (p.lse_out && c4 == 0) p.lse_out[orow] = den > 0.f ? (M + __log2f(den)) * kLn2 : neg_inf();
 }
 
-// Merge of split rows shaped to sit on an SM beside two row-kernel CTAs (128 threads, no
-// shared memory, <= 80 registers): its blocks become resident while the attention grid runs
-// and hold none of the slots the next call's attention CTAs take as this call's retire.
-// A block takes one (row, KV head) segment at a time: its 4 warps share the segment's piece
-// list (CTA boundaries found from the uniform split's guess c = x * n / U, corrected by
-// one or two loads) and each warp merges 4 of its query rows, one row per pass with every
-// piece's columns in flight.  Same log-sum-exp combination as decode_merge_kernel
-// (paged_kernel_v21.cuh:347-363).
-__device__ __forceinline__ int cta_of_near(const long long* cst, long long x, int n, long long U) {
-    int c = U > 0 ? (int)(x * n / U) : 0;
-    c = c < 0 ? 0 : (c > n - 1 ? n - 1 : c);
-    while (c > 0 && __ldg(cst + c) > x) --c;
-    while (c < n - 1 && __ldg(cst + c + 1) <= x) ++c;
-    return c;
-}
-
-template <class T, int E>
-__global__ void __launch_bounds__(128, 6) decode_merge_lite_kernel(PagedParams p) {
-    constexpr int NC = (E + 127) / 128;  // float4 columns per lane
-    constexpr int B = 12;                // pieces in flight per pass
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const DecodeSched sch = *p.sched;
-    const int n = sch.n_eff;
-    const float nan = __int_as_float(0x7fc00000);
-    for (int g_seg = blockIdx.x; g_seg < p.WS * p.Hkv; g_seg += gridDim.x) {
-        const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
-        const int w = ws / p.S, s = ws - w * p.S;
-        const long long P0 = __ldg(p.P + ws), V = __ldg(p.P + ws + 1) - P0;
-        for (int r = wid; r < p.gqa; r += 4) {
-            const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
-            T* op = static_cast<T*>(p.out) + orow * E;
-            if (sch.error || V == 0) {
-                const float z = sch.error ? nan : 0.f;
-#pragma unroll
-                for (int k = 0; k < NC; ++k)
-                    if (4 * lane + 128 * k < E) {
-                        store_quad<T>(op + 4 * lane + 128 * k, z, z, z, z);
-                        if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + 4 * lane + 128 * k) = make_float4(z, z, z, z);
-                    }
-                if (p.lse_out && lane == 0) p.lse_out[orow] = sch.error ? nan : neg_inf();
-            }
-        }
-        if (sch.error || V == 0) continue;
-        const long long b = P0 * p.hsplit + (p.hsplit > 1 ? hkv * V : 0);
-        const int ca = cta_of_near(p.cstart, b, n, sch.U), cb = cta_of_near(p.cstart, b + V - 1, n, sch.U);
-        if (ca == cb) continue;  // one piece: the attention kernel wrote the row
-        const int hh = p.slot_heads > 1 ? hkv : 0;
-        const bool ca_not_first = __ldg(p.cstart + ca) < b;
-        for (int r = wid; r < p.gqa; r += 4) {
-            float4 acc[NC];
-#pragma unroll
-            for (int k = 0; k < NC; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-            float M = neg_inf(), den = 0.f;
-            for (int c0 = ca; c0 <= cb; c0 += B) {
-                float l[B];
-                float4 v[B][NC];
-#pragma unroll
-                for (int j = 0; j < B; ++j) {
-                    const int cc = c0 + j;
-                    l[j] = neg_inf();
-#pragma unroll
-                    for (int k = 0; k < NC; ++k) v[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (cc <= cb && __ldg(p.cstart + cc) != __ldg(p.cstart + cc + 1)) {
-                        const int slot = (cc == ca && ca_not_first) ? 2 * ca + 1 : 2 * cc;
-                        const int pi = (slot * p.slot_heads + hh) * 16 + r;
-                        l[j] = p.part_lse[pi];
-#pragma unroll
-                        for (int k = 0; k < NC; ++k)
-                            if (4 * lane + 128 * k < E)
-                                v[j][k] = reinterpret_cast<const float4*>(p.part_o + (size_t)pi * E)[lane + 32 * k];
-                    }
-                }
-                float mb = M;
-#pragma unroll
-                for (int j = 0; j < B; ++j) mb = fmaxf(mb, l[j]);
-                if (mb == neg_inf()) continue;
-                const float sc = fast_exp2(M - mb);
-                den *= sc;
-#pragma unroll
-                for (int k = 0; k < NC; ++k) {
-                    acc[k].x *= sc; acc[k].y *= sc; acc[k].z *= sc; acc[k].w *= sc;
-                }
-#pragma unroll
-                for (int j = 0; j < B; ++j) {
-                    const float wj = fast_exp2(l[j] - mb);  // 0 for empty pieces
-                    den += wj;
-#pragma unroll
-                    for (int k = 0; k < NC; ++k) {
-                        acc[k].x += wj * v[j][k].x; acc[k].y += wj * v[j][k].y;
-                        acc[k].z += wj * v[j][k].z; acc[k].w += wj * v[j][k].w;
-                    }
-                }
-                M = mb;
-            }
-            const float inv = den > 0.f ? 1.f / den : 0.f;
-            const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
-#pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                if (4 * lane + 128 * k >= E) continue;
-                const float4 o = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
-                store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * lane + 128 * k, o.x, o.y, o.z, o.w);
-                if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + orow * E + 4 * lane + 128 * k) = o;
-            }
-            if (p.lse_out && lane == 0) p.lse_out[orow] = den > 0.f ? (M + __log2f(den)) * kLn2 : neg_inf();
-        }
-    }
-}
-
-// EXPERIMENT (timing only; outputs wrong): a merge that does nothing.
-template <int NTH, int SMEMB>
-__global__ void __launch_bounds__(NTH) decode_merge_empty_kernel(PagedParams p) {
-    __shared__ int pad[SMEMB / 4 + 1];
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (threadIdx.x == 0 && p.n_launch < 0) pad[0] = 1, p.sched->U = pad[0];
-}
-
 // Grid-stride over the (row, KV head) segments: few blocks, so that while they wait for
 // the attention grid they hold few of the slots the next call's attention CTAs need.
 template <class T, int E>
@@ -1922,7 +1778,6 @@ struct KernelChoice {
     bool row = false;  // all KV heads per CTA (hsplit = 1)
     int cw = 4;
     size_t sched_smem = 0;  // shared bytes the row kernel lends to its in-kernel schedule
-    size_t smem_one_warp_per_head = 0;  // row kernel launch size when Hkv == CW and the rotation is vectorised
 };
 
 template <class T, int E, int CW, int STAGES>
@@ -1932,7 +1787,6 @@ KernelChoice row_choice() {
     k.row = true;
     k.cw = CW;
     k.sched_smem = 2 * C::OFF_V;
-    k.smem_one_warp_per_head = C::SMEM_ONE_WARP_PER_HEAD;
     return k;
 }
 
@@ -2298,15 +2152,6 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     p.fused = (kc.row && !p.cu_q && (size_t)(p.WS + 1 + 32) * 8 <= kc.sched_smem &&
                (long long)p.WS + 1 <= 32LL * n_launch) ? 1 : 0;
     p.stall_tile = stall_tile_hook();
-    {
-        // EXPERIMENT switch: the row kernel with one warp per KV head launched without the
-        // merge-statistics / cos-sin staging area (vectorised rotation only)
-        const char* ex = getenv("DVB_EXP");
-        const bool vec_rot = (p.R / 2) % 8 == 0 && (p.cs_stride % 4) == 0 &&
-                             ((reinterpret_cast<uintptr_t>(p.cos) | reinterpret_cast<uintptr_t>(p.sin)) & 15) == 0;
-        p.small_smem = (ex && ex[0] && ex[0] != '0' && kc.row && p.Hkv == kc.cw && vec_rot) ? 1 : 0;
-        p.exp_nowait = (ex && ex[0] == '5') ? 1 : 0;
-    }
 
     // the first kernel this call launches may overlap the kernel before it only if that
     // kernel cannot have written this call's inputs (see first_launch_may_overlap)
@@ -2331,7 +2176,6 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         cfg.gridDim = dim3(n_launch);
         cfg.blockDim = dim3(kc.nt);
         cfg.dynamicSmemBytes = kc.smem;
-        if (p.small_smem) cfg.dynamicSmemBytes = kc.smem_one_warp_per_head;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -2392,23 +2236,6 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         const long long nseg = (long long)p.WS * p.Hkv;
         cfg.gridDim = dim3((unsigned)(nseg < DVB_MERGE_CTAS ? nseg : DVB_MERGE_CTAS));
         cfg.blockDim = dim3(16 * p.E / 4);
-        {
-            const char* ex = getenv("DVB_EXP");
-            if (ex && ex[0] == '1') {  // empty merge, 128 threads, no shared memory, 148 blocks
-                mk = (const void*)&decode_merge_empty_kernel<128, 0>;
-                cfg.gridDim = dim3(148);
-                cfg.blockDim = dim3(128);
-            } else if (ex && ex[0] == '2') {  // empty merge with the real merge's footprint
-                mk = (const void*)&decode_merge_empty_kernel<512, 10240>;
-                cfg.blockDim = dim3(512);
-            } else if (ex && (ex[0] == '4' || ex[0] == '5') && p.E == 128) {  // lite merge, co-resident
-                mk = dtype == DVATTN_BFLOAT16 ? (const void*)&decode_merge_lite_kernel<__nv_bfloat16, 128>
-                   : dtype == DVATTN_FLOAT16 ? (const void*)&decode_merge_lite_kernel<__half, 128>
-                                             : (const void*)&decode_merge_lite_kernel<float, 128>;
-                cfg.gridDim = dim3((unsigned)(nseg < 148 ? nseg : 148));
-                cfg.blockDim = dim3(128);
-            }
-        }
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

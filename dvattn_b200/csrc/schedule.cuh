@@ -90,10 +90,6 @@ struct PagedParams {
     // Test hook (DVATTN_TEST_STALL_TILE): the row kernel's CTA 0 never issues the loads of
     // this tile, so a bounded wait runs out and the call reports its error word; -1: off.
     int stall_tile;
-    // row kernel launched with RowCfg::SMEM_ONE_WARP_PER_HEAD bytes (one warp per KV head,
-    // vectorised rotation): it must not touch the merge-statistics / cos-sin staging area
-    int small_smem;
-    int exp_nowait;  // EXPERIMENT: consumers skip the wait before their first write (timing only)
 };
 
 

@@ -169,3 +169,26 @@ def test_split_kv_across_parts_equals_whole():
     capi.lse_merge(torch.stack(parts_o), torch.stack(parts_l), merged)
     torch.cuda.synchronize()
     assert_out_close(merged, whole.float(), torch.float16, "split-kv merge")
+
+
+def test_packed_merge_of_real_shards_equals_unsharded():
+    """Three KV-chunk shards of a real paged call write their partials through
+    dist.packed_partials; the buffers laid end to end (as one all-gather produces them)
+    merge with dvattn_lse_merge_packed to the unsharded call's output."""
+    from dvattn_b200 import dist as ddist
+    full = wl.make_paged([[3000], [1301], [64]], Hq=32, Hkv=2, E=128, R=64, BS=16, dtype=torch.bfloat16,
+                         seed=31).to(DEV)
+    ref = full.new_out()
+    capi.paged_sdpa(*full.op_args(ref))
+    parts = []
+    for r in range(3):
+        sh = ddist.kv_chunk_shard(full, r, 3, local_pages=True)
+        out = sh.new_out()
+        packed, o32, lse = ddist.packed_partials(out)
+        capi.paged_sdpa(*sh.op_args(out), lse=lse, out_f32=o32)
+        parts.append(packed)
+    gathered = torch.stack(parts).contiguous()
+    merged = torch.full_like(ref, float("nan"))
+    capi.lse_merge_packed(gathered, merged)
+    torch.cuda.synchronize()
+    assert_out_close(merged, ref.float(), torch.bfloat16, "packed merge of 3 real shards")

@@ -53,3 +53,20 @@ def test_noalloc_rejects_problems_beyond_the_scratch():
     assert need > cap
     assert capi.lib().dvattn_paged_sdpa_noalloc(ctypes.byref(a), torch.cuda.current_stream().cuda_stream) == \
         capi.DVATTN_ERR_WORKSPACE
+
+
+def test_noalloc_call_allocates_no_device_memory():
+    """After the first call on the device (which looks up the scratch address), further
+    calls change neither the torch allocator's statistics nor the device's free memory."""
+    c = wl.config2(W=8, device=DEV)
+    out = c.new_out()
+    assert _noalloc(c, out) == capi.DVATTN_OK
+    torch.cuda.synchronize()
+    before_stats = torch.cuda.memory_stats(DEV)["allocated_bytes.all.current"]
+    before_free = torch.cuda.mem_get_info(DEV)[0]
+    for _ in range(3):
+        assert _noalloc(c, out) == capi.DVATTN_OK
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_stats(DEV)["allocated_bytes.all.current"] == before_stats
+    assert torch.cuda.mem_get_info(DEV)[0] == before_free
+    assert capi.workspace_status(None) == 0
