@@ -7,21 +7,27 @@ R=64, KV lengths U[512, 8192] in two turns, page 16).  A step is one call of the
 one batch (one layer-step).  Metric: algorithmic HBM GB/s of the op (attended K/V rows +
 q + out + cos/sin + tables), and microseconds per layer-step.
 
-* value: device-resident inputs, K calls of the C ABI (libdvattn_b200.so) timed with CUDA
-  events on the launching stream; between steps the call rotates over three copies of
-  the KV page pool (each larger than the 126 MB L2), so no step reads K/V from L2 left by
-  the previous one.
+* value: device-resident inputs, K calls of the C ABI (libdvattn_b200.so) captured once
+  in a CUDA graph and replayed, timed with CUDA events on the launching stream; the rep
+  of K steps is repeated (>= 25 reps, ~1 s) and the median rep is reported with its
+  spread; between steps the call rotates over three copies of the KV page pool (each
+  larger than the 126 MB L2), so no step reads K/V from L2 left by the previous one.
 * e2e: the same metric through the public torch op (torch.ops.libdvatt.dvattn_paged_sdpa)
-  with the step's inputs (q, cos/sin, locations, fragment lengths, block tables) copied
-  from pinned host memory and the output copied back inside the timed region; the KV
-  cache stays resident, as in a serving engine.
+  with every step's inputs (q, cos/sin, locations, fragment lengths, block tables) copied
+  from pinned host memory and its output copied back inside the timed region (H2D issued
+  in groups of 4 steps ahead of the compute, D2H right after each op); the KV cache stays
+  resident, as in a serving engine.
 * roofline: the attention kernel alone (C-ABI phase ATTEND between CUDA events), against
   the measured HBM copy bandwidth of MEASURED_PEAKS.json.
 * cpu_baseline: the reference's pure-PyTorch path (oracle restatement of
   dvattn_sdpa_pt + apply_rotary_pos_emb) on a bounded sample, on rank 0 only.
-* Multi-GPU (torchrun): weak scaling -- every rank decodes its own batch of the same
-  shape, no collective on the data path; value = all ranks' bytes / max-over-ranks time.
-  --workload long3: config 3 KV-chunk-sharded across ranks + NCCL all-gather LSE merge.
+* strong_scaling (default workload): config 2's batch split over the ranks (N > 1), and
+  config 3's long context split by KV chunk with the partials exchanged over peer memory
+  (dvattn_lse_merge_peers; the NCCL all-gather path timed beside it), each with its
+  efficiency against the same work on one GPU.
+* Multi-GPU (torchrun): value is weak scaling -- every rank decodes its own batch of the
+  same shape, no collective on the data path; value = all ranks' bytes / max-over-ranks
+  time.  --workload long3: config 3 KV-chunk-sharded alone, one JSON line.
 """
 from __future__ import annotations
 
