@@ -15,7 +15,7 @@ q + out + cos/sin + tables), and microseconds per layer-step.
 * e2e: the same metric through the public torch op (torch.ops.libdvatt.dvattn_paged_sdpa)
   with every step's inputs (q, cos/sin, locations, fragment lengths, block tables) copied
   from pinned host memory and its output copied back inside the timed region (H2D issued
-  in groups of 4 steps ahead of the compute, D2H right after each op); the KV cache stays
+  in groups of 1, 2, 4, 8 steps ahead of the compute, D2H right after each op); the KV cache stays
   resident, as in a serving engine.
 * roofline: the attention kernel alone (C-ABI phase ATTEND between CUDA events), against
   the measured HBM copy bandwidth of MEASURED_PEAKS.json.
@@ -143,17 +143,28 @@ def traffic_from_profiles(workload: str):
     return None
 
 
-def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 4):
+def group_starts(nsteps: int, cap: int):
+    """Step indices where the H2D groups start: sizes 1, 2, 4, ... up to `cap`, so the first
+    group (whose copy nothing can hide) is short and later ones amortise their wait."""
+    starts, i, size = [], 0, 1
+    while i < nsteps:
+        starts.append(i)
+        i += size
+        size = min(cap, size * 2)
+    return starts + [nsteps]
+
+
+def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 8):
     """End-to-end step time through a public API with host inputs and a host result, run
     the way a serving loop runs it: every step's inputs (pinned host tensors, packed into
     one buffer) go to the device in ONE copy on an H2D stream, the op runs on the compute
     stream, and every step's output comes back to pinned host memory on a D2H stream right
-    after its op.  The H2D copies are issued in groups of `group` steps, one group ahead of
-    the compute, and the compute stream waits once per group (a wait in front of a kernel
-    costs it the programmatic overlap with the kernel before it, so the waits are batched);
-    device buffers form a ring of whole groups; the K steps are captured once in a CUDA
-    graph and replayed.  Every step's H2D and D2H copy is inside the timed region.
-    `launch(dev_inputs, out, i)` enqueues the op on the current stream.
+    after its op.  The H2D copies are issued in groups of 1, 2, 4, ... up to `group` steps,
+    one group ahead of the compute, and the compute stream waits once per group (a wait in
+    front of a kernel costs it the programmatic overlap with the kernel before it, so the
+    waits are batched); device buffers form a ring of at least two groups; the K steps are
+    captured once in a CUDA graph and replayed.  Every step's H2D and D2H copy is inside the
+    timed region.  `launch(dev_inputs, out, i)` enqueues the op on the current stream.
     Returns (ms per step, H2D bytes, D2H bytes per step, mode)."""
     dev = out_like.device
     sizes = [t.numel() * t.element_size() for t in host_in]
@@ -165,10 +176,10 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 
     for t, o, b in zip(host_in, offs, sizes):
         host_flat[o:o + b].copy_(t.contiguous().reshape(-1).view(torch.uint8))
     out_b = out_like.numel() * out_like.element_size()
-    # device buffers: a ring of R steps (a multiple of the group, at least two groups), all
-    # K steps when they fit in ~1 GB
+    # device buffers: a ring of R steps (at least two of the largest groups), all K steps
+    # when they fit in ~1 GB
     fit = max(1, (1 << 30) // (n + out_b))
-    R = max(2 * group, min(steps + (-steps) % group, fit // group * group))
+    R = max(2 * group, min(steps, fit))
     dev_flat = torch.empty((R, n), dtype=torch.uint8, device=dev)
     views = [[dev_flat[k][o:o + b].view(t.dtype).view(t.shape) for t, o, b in zip(host_in, offs, sizes)]
              for k in range(R)]
@@ -180,15 +191,16 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 
         main = torch.cuda.current_stream()
         h2d_s.wait_stream(main)
         d2h_s.wait_stream(main)
-        ngroups = -(-nsteps // group)
+        st = group_starts(nsteps, group)
+        ngroups = len(st) - 1
         ev_in, ev_op, ev_d2h = [None] * ngroups, [None] * nsteps, [None] * nsteps
 
         def issue_h2d(g):
             with torch.cuda.stream(h2d_s):
-                reuse = g * group + group - 1 - R  # last op that read these input buffers
+                reuse = st[g + 1] - 1 - R  # last op that read these input buffers
                 if reuse >= 0:
                     h2d_s.wait_event(ev_op[reuse])
-                for i in range(g * group, min(g * group + group, nsteps)):
+                for i in range(st[g], st[g + 1]):
                     dev_flat[i % R].copy_(host_flat, non_blocking=True)
                 ev_in[g] = torch.cuda.Event()
                 ev_in[g].record(h2d_s)
@@ -198,10 +210,10 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 
             if g + 1 < ngroups:
                 issue_h2d(g + 1)  # one group ahead of the compute
             main.wait_event(ev_in[g])
-            reuse = g * group + group - 1 - R  # last D2H that read these output buffers
+            reuse = st[g + 1] - 1 - R  # last D2H that read these output buffers
             if reuse >= 0:
                 main.wait_event(ev_d2h[reuse])
-            for i in range(g * group, min(g * group + group, nsteps)):
+            for i in range(st[g], st[g + 1]):
                 launch(views[i % R], outs[i % R], i)
                 ev_op[i] = torch.cuda.Event()
                 ev_op[i].record(main)
@@ -215,7 +227,7 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 
 
     run(warmup)
     torch.cuda.synchronize()
-    mode = f"cuda-graph, H2D in groups of {group} steps"
+    mode = f"cuda-graph, H2D in groups of 1, 2, 4, ... {group} steps"
     graph = None
     try:
         graph = torch.cuda.CUDAGraph()
@@ -224,7 +236,7 @@ def pipelined_e2e(host_in, out_like, launch, steps, warmup, world, group: int = 
         graph.replay()
         torch.cuda.synchronize()
     except Exception:  # capture unsupported for this op: issue eagerly
-        graph, mode = None, f"eager, H2D in groups of {group} steps"
+        graph, mode = None, f"eager, H2D in groups of 1, 2, 4, ... {group} steps"
         torch.cuda.synchronize()
     barrier(world)
     main = torch.cuda.current_stream()
@@ -614,8 +626,9 @@ def run_ours(args, world, rank, local):
                          "frac_back_to_back": round(nbytes / (kb_ms * 1e-3) / 1e9 / hbm_peak, 4)},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "us_per_layer_step": round(e2e_ms * 1e3, 2), "api": "torch.ops.libdvatt.dvattn_paged_sdpa", "issue": e2e_mode,
-                    "copies": "per step one packed H2D of its inputs (issued in groups of 4 steps ahead of the "
-                              "compute) and one D2H of its output right after its op, on copy streams"},
+                    "copies": "per step one packed H2D of its inputs (issued in groups of 1, 2, 4, 8 steps, "
+                              "one group ahead of the compute) and one D2H of its output right after its op, on "
+                              "copy streams"},
             "gpu_launches": launches_per_step * args.steps * len(per_rep),
             "gpu_launches_per_step": launches_per_step,
             "clocks": clocks,

@@ -1647,22 +1647,39 @@ __global__ void __launch_bounds__(128) decode_f32_kernel(PagedParams p) {
 // one CTA per segment, 128 threads: thread t -> row t/8, columns 4*((t%8) + 8k)
 // ==================================================================================
 
-// Merge of one (row, KV head) segment, one thread per (query row r, 4-column group c4):
-// blockDim = 16 * E / 4; all threads of the block call it with the same segment.  Pieces
-// are consumed in batches of 16 whose loads are all in flight before any is used (the
-// merge is latency-bound, not bandwidth-bound).
+// Thread layout of the merge: TPR threads per query row, each owning NC 4-column groups
+// (c4, c4 + TPR, ...), 16 rows per block; pieces are loaded B at a time.  Up to E = 128 a
+// thread owns one group; at E = 256 two, so the block stays at 512 threads and the B * NC
+// values in flight fit in registers (a 1024-thread block would get 64 and spill).
+template <int E>
+struct MergeCfg {
+    static constexpr int C4 = E / 4;
+    static constexpr int TPR = C4 < 32 ? C4 : 32;
+    static constexpr int NC = C4 / TPR;
+    static constexpr int NTH = 16 * TPR;
+    static constexpr int B = 16 / NC;
+};
+
+// Merge of one (row, KV head) segment; all threads of the block call it with the same
+// segment.  Pieces are consumed in batches of B whose loads are all in flight before any
+// is used (the merge is latency-bound, not bandwidth-bound).
 template <class T, int E>
 __device__ __forceinline__ void merge_segment(const PagedParams& p, int g_seg, const long long* cst, int n, int* s_part) {
-    constexpr int C4 = E / 4, NTH = 16 * C4, B = 16;
+    using MC = MergeCfg<E>;
+    constexpr int TPR = MC::TPR, NC = MC::NC, NTH = MC::NTH, B = MC::B;
     const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
-    const int tid = threadIdx.x, r = tid / C4, c4 = tid - r * C4;
+    const int tid = threadIdx.x, r = tid / TPR, c4 = tid - r * TPR;
     const long long P0 = p.P[ws], V = p.P[ws + 1] - P0;
     const int w = ws / p.S, s = ws - w * p.S;
     const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
     if (V == 0) {
         if (r < p.gqa) {
-            store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, 0.f, 0.f, 0.f, 0.f);
-            if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                const int q = c4 + TPR * k;
+                store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * q, 0.f, 0.f, 0.f, 0.f);
+                if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
             if (p.lse_out && c4 == 0) p.lse_out[orow] = neg_inf();
         }
         return;
@@ -1673,7 +1690,9 @@ __device__ __forceinline__ void merge_segment(const PagedParams& p, int g_seg, c
     const int npc = cb - ca + 1;
     const int hh = p.slot_heads > 1 ? hkv : 0;
     const bool ca_not_first = cst[ca] < b;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 acc[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     float M = neg_inf(), den = 0.f;
     for (int base = 0; base < npc; base += NTH) {
         const int cnt = min(NTH, npc - base);
@@ -1688,15 +1707,18 @@ __device__ __forceinline__ void merge_segment(const PagedParams& p, int g_seg, c
         if (r >= p.gqa) continue;
         for (int k0 = 0; k0 < cnt; k0 += B) {
             float l[B];
-            float4 v[B];
+            float4 v[B][NC];
 #pragma unroll
             for (int j = 0; j < B; ++j) {
                 l[j] = neg_inf();
-                v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int k = 0; k < NC; ++k) v[j][k] = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (k0 + j < cnt && s_part[k0 + j] >= 0) {
                     const int pi = s_part[k0 + j] + r;
                     l[j] = p.part_lse[pi];
-                    v[j] = reinterpret_cast<const float4*>(p.part_o + (size_t)pi * E)[c4];
+#pragma unroll
+                    for (int k = 0; k < NC; ++k)
+                        v[j][k] = reinterpret_cast<const float4*>(p.part_o + (size_t)pi * E)[c4 + TPR * k];
                 }
             }
             float mb = M;
@@ -1705,29 +1727,40 @@ __device__ __forceinline__ void merge_segment(const PagedParams& p, int g_seg, c
             if (mb == neg_inf()) continue;
             const float sc = fast_exp2(M - mb);
             den *= sc;
-            acc.x *= sc; acc.y *= sc; acc.z *= sc; acc.w *= sc;
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                acc[k].x *= sc; acc[k].y *= sc; acc[k].z *= sc; acc[k].w *= sc;
+            }
 #pragma unroll
             for (int j = 0; j < B; ++j) {
                 const float wj = fast_exp2(l[j] - mb);  // 0 for empty pieces
                 den += wj;
-                acc.x += wj * v[j].x; acc.y += wj * v[j].y; acc.z += wj * v[j].z; acc.w += wj * v[j].w;
+#pragma unroll
+                for (int k = 0; k < NC; ++k) {
+                    acc[k].x += wj * v[j][k].x; acc[k].y += wj * v[j][k].y;
+                    acc[k].z += wj * v[j][k].z; acc[k].w += wj * v[j][k].w;
+                }
             }
             M = mb;
         }
     }
     if (r >= p.gqa) return;
     const float inv = den > 0.f ? 1.f / den : 0.f;
-    acc.x *= inv; acc.y *= inv; acc.z *= inv; acc.w *= inv;
-    store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, acc.x, acc.y, acc.z, acc.w);
-    if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = acc;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int q = c4 + TPR * k;
+        const float4 o = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
+        store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * q, o.x, o.y, o.z, o.w);
+        if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[q] = o;
+    }
     if (p.lse_out && c4 == 0) p.lse_out[orow] = den > 0.f ? (M + __log2f(den)) * kLn2 : neg_inf();
 }
 
 // Grid-stride over the (row, KV head) segments: few blocks, so that while they wait for
 // the attention grid they hold few of the slots the next call's attention CTAs need.
 template <class T, int E>
-__global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p) {
-    constexpr int NTH = 16 * (E / 4);
+__global__ void __launch_bounds__(MergeCfg<E>::NTH) decode_merge_kernel(PagedParams p) {
+    constexpr int NTH = MergeCfg<E>::NTH;
     // launched as a programmatic dependent of the attention kernel: wait for its results
     // let the next call's schedule kernel start its (read-only) work now
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1747,12 +1780,15 @@ __global__ void __launch_bounds__(16 * E / 4) decode_merge_kernel(PagedParams p)
         const float nan = __int_as_float(0x7fc00000);
         for (int g_seg = blockIdx.x; g_seg < p.WS * p.Hkv; g_seg += gridDim.x) {
             const int ws = g_seg / p.Hkv, hkv = g_seg - ws * p.Hkv;
-            const int r = tid / (E / 4), c4 = tid - r * (E / 4);
+            constexpr int TPR = MergeCfg<E>::TPR;
+            const int r = tid / TPR, c4 = tid - r * TPR;
             if (r >= p.gqa) continue;
             const int w = ws / p.S, s = ws - w * p.S;
             const size_t orow = ((size_t)w * p.Hq + hkv * p.gqa + r) * p.S + s;
-            store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * c4, nan, nan, nan, nan);
-            if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[c4] = make_float4(nan, nan, nan, nan);
+            for (int q = c4; q < E / 4; q += TPR) {
+                store_quad<T>(static_cast<T*>(p.out) + orow * E + 4 * q, nan, nan, nan, nan);
+                if (p.out_f32) reinterpret_cast<float4*>(p.out_f32 + orow * E)[q] = make_float4(nan, nan, nan, nan);
+            }
             if (p.lse_out && c4 == 0) p.lse_out[orow] = nan;
         }
         return;
@@ -2235,7 +2271,7 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
         // call's attention CTAs need while they wait for this call's attention grid
         const long long nseg = (long long)p.WS * p.Hkv;
         cfg.gridDim = dim3((unsigned)(nseg < DVB_MERGE_CTAS ? nseg : DVB_MERGE_CTAS));
-        cfg.blockDim = dim3(16 * p.E / 4);
+        cfg.blockDim = dim3(p.E == 64 ? MergeCfg<64>::NTH : p.E == 128 ? MergeCfg<128>::NTH : MergeCfg<256>::NTH);
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
