@@ -592,9 +592,18 @@ def run_ours(args, world, rank, local):
     if args.workload == "config2" and not args.no_extra:
         # strong scaling (same total work at every N): the batch split over the ranks, and
         # config 3's long context split by KV chunk with its NCCL exchange
-        if world > 1:
-            extra["config2_batch"] = batch_strong_scaling(case, world, rank, args.steps)
-        extra["long3"] = long3_scaling(world, rank, dev, args.steps)
+        # a failing leg is reported in the line instead of ending the run (both legs make
+        # the same collective calls on every rank, so a failure is seen by all of them)
+        for key, fn in (("config2_batch", (lambda: batch_strong_scaling(case, world, rank, args.steps))
+                         if world > 1 else None),
+                        ("long3", lambda: long3_scaling(world, rank, dev, args.steps))):
+            if fn is None:
+                continue
+            try:
+                extra[key] = fn()
+            except Exception as e:  # noqa: BLE001
+                torch.cuda.synchronize()
+                extra[key] = {"error": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
