@@ -351,24 +351,44 @@ def sum_over_ranks(x: float, world: int) -> float:
 # ------------------------------------------------------------------------------------
 # CPU baseline: the reference's pure-PyTorch path on a bounded sample
 # ------------------------------------------------------------------------------------
-def cpu_sample_gbs(case_fn, n_seq: int, reps: int = 3):
-    """Time oracle.paged_via_sdpa_pt (dvattn_sdpa_pt + apply_rotary_pos_emb restated) on the
-    first n_seq sequences of the workload; returns (GB/s, threads, description)."""
+def reference_cpu_work(name: str):
+    """The reference's CPU path on workload `name`: (list of call argument tuples for
+    oracle.paged_via_sdpa_pt, the case, same_config, description).  Configs 1 and 2 run
+    whole, one reference call per sequence with its fragments cut at the sequence's own
+    visible length; the larger configs run on a bounded sample."""
+    wl = _wl()
+    if name in ("config1", "config2"):
+        c = wl.config1() if name == "config1" else wl.config2()
+        W = c.queries.size(0)
+        subs = [(c.scale, c.locations[:, w:w + 1], c.queries[w:w + 1], c.cosines[:, w:w + 1], c.sines[:, w:w + 1],
+                 c.fragment_lengths, c.k_cache, c.v_cache, c.block_tables[w:w + 1]) for w in range(W)]
+        return subs, c, True, f"the whole workload ({W} sequences, one reference call per sequence)"
+    n, desc = CPU_SAMPLE[name]
+    c = cpu_case_fn(name)(n)
+    return [(c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
+             c.block_tables)], c, False, desc
+
+
+def cpu_sample_gbs(name: str, reps: int = 3):
+    """Time the reference's CPU path (reference_cpu_work) on the host cores; returns
+    (GB/s, threads, description)."""
     from oracle import dvattn_oracle as O
     wl = _wl()
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    c = case_fn(n_seq)
-    args = (c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
-            c.block_tables)
-    O.paged_via_sdpa_pt(*args)  # warm-up (also the page gather)
+    subs, c, _, desc = reference_cpu_work(name)
+
+    def step():
+        for a in subs:
+            O.paged_via_sdpa_pt(*a, trim=True)
+
+    step()  # warm-up (also the page gather)
     ts = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        O.paged_via_sdpa_pt(*args)
+        step()
         ts.append(time.perf_counter() - t0)
-    t = statistics.median(ts)
-    return wl.paged_bytes(c) / t / 1e9, threads, t
+    return wl.paged_bytes(c) / statistics.median(ts) / 1e9, threads, desc
 
 
 # ------------------------------------------------------------------------------------
@@ -421,21 +441,9 @@ def run_reference(args, world, rank):
     from oracle import dvattn_oracle as O
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    if name in ("config1", "config2"):
-        c = wl.config1() if name == "config1" else wl.config2()
-        same = True
-        W = c.queries.size(0)
-        # one reference call per sequence, each sequence's fragments cut at its own
-        # visible length (a caller of the eager path holds per-sequence fragments)
-        subs = [(c.scale, c.locations[:, w:w + 1], c.queries[w:w + 1], c.cosines[:, w:w + 1], c.sines[:, w:w + 1],
-                 c.fragment_lengths, c.k_cache, c.v_cache, c.block_tables[w:w + 1]) for w in range(W)]
-        desc = f"the whole workload ({W} sequences, one reference call per sequence)"
-    else:
-        n, desc = CPU_SAMPLE[name]
-        c = cpu_case_fn(name)(n)
-        same = False
-        subs = [(c.scale, c.locations, c.queries, c.cosines, c.sines, c.fragment_lengths, c.k_cache, c.v_cache,
-                 c.block_tables)]
+    # one reference call per sequence, each sequence's fragments cut at its own visible
+    # length (a caller of the eager path holds per-sequence fragments)
+    subs, c, same, desc = reference_cpu_work(name)
 
     def step():
         for a in subs:
@@ -607,8 +615,7 @@ def run_ours(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        n, sdesc = CPU_SAMPLE[args.workload]
-        gbs, threads, _ = cpu_sample_gbs(cpu_case_fn(args.workload), n)
+        gbs, threads, sdesc = cpu_sample_gbs(args.workload)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sdesc}
     if rank == 0:
         traffic = traffic_from_profiles(args.workload)
