@@ -969,6 +969,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     const int c = blockIdx.x;
     long long u0, u1, P0, U = 0, pubP = 0;
     int ws0, n = 0;
+    long long bseg = -1;  // first segment start inside (u0, u1) when p.rotate (else none)
+    int wsb = 0;
     // fused schedule, producer warp: after the previous grid completed, publish P, cstart
     // and the header for the merge kernel
     auto publish = [&]() {
@@ -997,6 +999,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         u1 = cta_boundary(p, sP, U, n, c + 1);
         ws0 = u0 < u1 ? find_row_in(sP, p.WS, p.hsplit, u0) : 0;
         P0 = sP[ws0];
+        if (p.rotate && u0 < u1 && ws0 < p.WS) {
+            bseg = sP[ws0 + 1] * p.hsplit;
+            if (bseg > u0 && bseg < u1) wsb = find_row_in(sP, p.WS, p.hsplit, bseg);
+        }
         // this CTA publishes P[32c .. 32c+31] (producer warp lanes)
         if (wid == CW && 32 * c + lane <= p.WS) pubP = sP[32 * c + lane];
         __syncthreads();
@@ -1014,6 +1020,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
         if (u0 >= u1) return;
         ws0 = find_row<C::NT>(p, u0);
         P0 = p.P[ws0];
+        if (p.rotate && ws0 < p.WS) {
+            bseg = p.P[ws0 + 1] * p.hsplit;
+            if (bseg > u0 && bseg < u1) wsb = find_row<C::NT>(p, bseg);
+        }
     }
 
     if (tid == 0) {
@@ -1032,9 +1042,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
         }
-        TileIter<64> it;
-        it.init(p, ws0, P0, u0, u1);
-        it.align = TOKB;
+        RotTileIter<64> it;
+        it.init(p, ws0, P0, u0, u1, wsb, bseg, TOKB);
         struct Pend {
             TileDesc d;
             int pfirst, npg, page;
@@ -1162,9 +1171,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, (CW <= 4 && E <= 128) ? 2 : 1)
     // The first tile always starts a turn: rotate its q now, while the first stage's TMA
     // loads are in flight, instead of after they land.
     {
-        TileIter<64> it0;
-        it0.init(p, ws0, P0, u0, u1);
-        it0.align = TOKB;
+        RotTileIter<64> it0;
+        it0.init(p, ws0, P0, u0, u1, wsb, bseg, TOKB);
         TileDesc d0;
         if (it0.next(p, d0)) {
             rotate_q_inplace<T, E>(p, d0.ws, d0.f, Hkv, sQ, tid, CW * 32,
@@ -2182,12 +2190,19 @@ static int run_schedule(PagedParams p, int dtype, void* workspace, size_t wbytes
     }
     p.n_launch = n_launch;
     p.min_units = kc.min_units;
+    {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return DVATTN_ERR_CUDA;
+        p.n_sm = sms;
+        p.unit_bytes = (long long)(kc.row ? p.Hkv : 1) * 2 * p.E * esz;
+    }
     // Row kernel on paged decode: the split is computed inside the attention kernel (its
     // stages hold the prefix sums; CTA c publishes P[32c..32c+31] for the merge), so no
     // prep kernel runs and a call's streaming starts while the previous call's merge runs.
     p.fused = (kc.row && !p.cu_q && (size_t)(p.WS + 1 + 32) * 8 <= kc.sched_smem &&
                (long long)p.WS + 1 <= 32LL * n_launch) ? 1 : 0;
     p.stall_tile = stall_tile_hook();
+    p.rotate = kc.row ? 1 : 0;
 
     // the first kernel this call launches may overlap the kernel before it only if that
     // kernel cannot have written this call's inputs (see first_launch_may_overlap)

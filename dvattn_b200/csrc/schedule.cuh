@@ -90,6 +90,9 @@ struct PagedParams {
     // Test hook (DVATTN_TEST_STALL_TILE): the row kernel's CTA 0 never issues the loads of
     // this tile, so a bounded wait runs out and the call reports its error word; -1: off.
     int stall_tile;
+    int n_sm;        // SMs of the device (0: no one-wave cap)
+    long long unit_bytes;  // K+V bytes streamed per unit
+    int rotate;  // row kernel: walk each CTA's range from its first segment start (RotTileIter)
 };
 
 
@@ -168,9 +171,16 @@ __device__ __forceinline__ long long cta_boundary(const PagedParams& p, const lo
 }
 
 // Number of CTAs that own units: ceil(U / min_units) capped at n_launch (>= 1 if U > 0).
+// A call streaming less than kOneWaveBytes is further capped at one CTA per SM (p.n_sm):
+// with two per SM its rows split into twice as many pieces whose partials and merge cost
+// more than the second CTA's overlap gains (config 2 at 8 sequences: 36.3 -> 29.7 µs per
+// call; at 4: 33.0 -> 22-27 µs; from 16 sequences up, 2 per SM is as fast or faster).
+constexpr long long kOneWaveBytes = 96ll << 20;
 __device__ __forceinline__ int sched_ctas(const PagedParams& p, long long U) {
     const long long want = (U + p.min_units - 1) / p.min_units;
-    int n = (int)(want < p.n_launch ? want : p.n_launch);
+    int cap = p.n_launch;
+    if (p.n_sm > 0 && p.unit_bytes > 0 && U * p.unit_bytes < kOneWaveBytes && p.n_sm < cap) cap = p.n_sm;
+    int n = (int)(want < cap ? want : cap);
     return U > 0 ? (n > 0 ? n : 1) : 0;
 }
 
@@ -411,6 +421,44 @@ template <int TILE> struct TileIter {
         d.seg_complete = from_start && (seg_left == 0);
         pend_seg = pend_turn = false;
         return true;
+    }
+};
+
+// A CTA's unit range [u0, u1) walked from the first segment start b inside it: first
+// [b, u1), then [u0, b).  The piece [u0, b) -- the tail of a segment an earlier CTA began --
+// comes last, so every piece whose result is only a partial ends at the end of the CTA's
+// work, and its first global write comes after nearly all its streaming (the writes wait
+// for the previous grid, which may still be merging the previous call).  Slots keep their
+// meaning: [u0, b) is the CTA's first segment (first_piece), the rest are not.  Without a
+// segment start strictly inside the range this is the plain walk of [u0, u1).
+template <int TILE> struct RotTileIter {
+    TileIter<TILE> it;
+    int phase, ws0, align;
+    long long P0, u0, b;
+    __device__ __forceinline__ void init(const PagedParams& p, int ws0_, long long P0_, long long u0_, long long u1,
+                                         int wsb, long long b_, int align_) {
+        ws0 = ws0_;
+        P0 = P0_;
+        u0 = u0_;
+        b = b_;
+        align = align_;
+        if (b > u0 && b < u1) {
+            phase = 0;
+            it.init(p, wsb, b / p.hsplit, b, u1);
+            it.first_seg = false;
+        } else {
+            phase = 1;
+            it.init(p, ws0, P0, u0, u1);
+        }
+        it.align = align;
+    }
+    __device__ __forceinline__ bool next(const PagedParams& p, TileDesc& d) {
+        if (it.next(p, d)) return true;
+        if (phase != 0) return false;
+        phase = 1;
+        it.init(p, ws0, P0, u0, b);
+        it.align = align;
+        return it.next(p, d);
     }
 };
 
