@@ -5,7 +5,9 @@
 // a 128-row tile holds 128 / G consecutive tokens (row = j * G + g), and the item holds
 // two such tiles, A and B.  It streams the sequence's visible keys of every turn in
 // 128-key windows:
-//   warp 8      producer: block-table lookups + 3-D TMA page boxes into a 2-stage ring
+//   warps 8, 10 producers of K and of V: 3-D TMA page boxes into a 3-stage K and a
+//               2-stage V ring; the block-table entries of each window are fetched three
+//               windows early by cp.async into a small shared-memory ring
 //   warp 9      MMA issuer (one thread): S_A = Q_A K^T, S_B = Q_B K^T into TMEM, then
 //               O_A += P_A V, O_B += P_B V with P read from TMEM; completion is signalled
 //               by tcgen05.commit on mbarriers.  Issue order S_A(i), PV_B(i-1), S_B(i),
@@ -45,9 +47,13 @@ constexpr size_t OFF_K = OFF_Q + 2 * TILE;
 constexpr size_t OFF_V = OFF_K + KSTAGES * TILE;
 constexpr size_t OFF_BAR = OFF_V + VSTAGES * TILE;  // 24 mbarrier slots
 constexpr size_t OFF_MISC = OFF_BAR + 24 * 8;       // tmem base, abort flag
-constexpr size_t SMEM = OFF_MISC + 64;
-constexpr int NT = 10 * 32;
-constexpr int WARP_PRODUCER = 8, WARP_MMA = 9;
+constexpr size_t OFF_BT = OFF_MISC + 64;  // per producer warp: block-table entries of upcoming windows [8][16]
+constexpr size_t SMEM = OFF_BT + 2 * 8 * 16 * 4;
+constexpr int BT_AHEAD = 3;               // windows whose block-table entries are in flight
+static_assert(SMEM <= 232448, "prefill shared memory exceeds the 227 KB a CTA may use");
+constexpr int NT = 11 * 32;
+// producer warps 8 (K) and 10 (V), MMA warp 9
+constexpr int WARP_PRODUCER = 8, WARP_MMA = 9, WARP_PRODUCER_V = 10;
 
 struct Item {
     int w, t0, nt, hkv;
@@ -365,70 +371,88 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (wid == WARP_PRODUCER) {
+    if (wid == WARP_PRODUCER || wid == WARP_PRODUCER_V) {
         // =============================== producer ===============================
         if (lane == 0) {
             prefetch_tmap(&tmk);
             prefetch_tmap(&tmv);
         }
         const int* btw = p.bt + (size_t)it.w * p.maxb;
-        const int pages = KT / p.BS;
-        // one 128-key window of K or V: a 3-D box {64 columns, 1 head, BS rows} per page
-        // and 64-column panel; pages outside the window's needed range, outside the block
-        // table or the pool load as zeros (out-of-bounds coordinate)
-        auto load = [&](const TileSeq& q, const CUtensorMap* map, uint32_t dst, uint32_t fullbar) {
+        const int pages = KT / p.BS;  // one page per lane (at most 16)
+        // A 128-key window is a 3-D box {64 columns, 1 head, BS rows} per page and 64-column
+        // panel; pages outside the window's needed range, outside the block table or the
+        // pool load as zeros (out-of-bounds coordinate).  The block-table entries of window
+        // w are fetched BT_AHEAD windows early by cp.async into a shared-memory ring (one
+        // commit group per window), so their latency stays off the producer's path.
+        const uint32_t bt_ring = (uint32_t)(OFF_BT + (wid == WARP_PRODUCER ? 0 : 512));
+        auto needed = [&](const TileSeq& q, int& pos) {
+            pos = q.win + lane * p.BS;
+            return lane < pages && pos + p.BS > q.off && pos < q.off + q.vmax && (pos / p.BS) < p.maxb;
+        };
+        auto prefetch = [&](const TileSeq& q, int w) {
+            int pos;
+            if (q.valid && needed(q, pos)) {
+                const uint32_t dst = s0 + bt_ring + (uint32_t)(((w & 7) * 16 + lane) * 4);
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(btw + pos / p.BS) : "memory");
+            }
+            cp_async_commit();
+        };
+        auto coord = [&](const TileSeq& q, int w) {  // after window w's group completed
+            int pos;
+            if (!needed(q, pos)) return -2 * p.BS;
+            const int page = reinterpret_cast<const int*>(smem + bt_ring)[(w & 7) * 16 + lane];
+            return page >= 0 && page < p.NB ? page * p.BS : -2 * p.BS;
+        };
+        auto load = [&](const CUtensorMap* map, uint32_t dst, uint32_t fullbar, int z) {
             if (lane == 0) mbar_expect_tx(fullbar, (uint32_t)TILE);
             __syncwarp();
-            for (int j = lane; j < pages; j += 32) {
-                const int pos = q.win + j * p.BS;  // first logical position of page j
-                const bool need = pos + p.BS > q.off && pos < q.off + q.vmax && (pos / p.BS) < p.maxb;
-                const int page = need ? __ldg(btw + pos / p.BS) : -1;
-                const bool valid = need && page >= 0 && page < p.NB;
-                const int z = valid ? page * p.BS : -2 * p.BS;
-                const uint32_t d = dst + (uint32_t)(j * p.BS * 128);
+            if (lane < pages) {
+                const uint32_t d = dst + (uint32_t)(lane * p.BS * 128);
                 tma_load_3d(d, map, 0, it.hkv, z, fullbar);
                 tma_load_3d(d + PANEL, map, 64, it.hkv, z, fullbar);
             }
         };
-        // K runs one window ahead of V: K(i+1) frees (S of window i-2 done) before V(i)
-        // does (PV of window i-2 done)
-        TileSeq kq, vq;
+        // Warp 8 streams K, warp 10 V, each window into its ring once the window KSTAGES
+        // (VSTAGES) before it has been consumed: issuing the 2 x 8 page boxes of a window
+        // keeps one warp busy for about as long as the MMAs of half a window take.
+        const bool is_k = wid == WARP_PRODUCER;
+        const int nst = is_k ? KSTAGES : VSTAGES;
+        const uint32_t fullb = is_k ? k_full : v_full, emptyb = is_k ? k_empty : v_empty;
+        const uint32_t ring = s0 + (uint32_t)(is_k ? OFF_K : OFF_V);
+        const CUtensorMap* map = is_k ? &tmk : &tmv;
+        TileSeq kq, la;
         kq.init(p, it, lane);
-        vq.init(p, it, lane);
-        int ik = 0, iv = 0;
+        la.init(p, it, lane);
+        for (int w = 0; w < BT_AHEAD; ++w) {
+            prefetch(la, w);
+            if (la.valid) la.next(p, it, lane);
+        }
+        int ik = 0;
         bool ok = true;
-        while (vq.valid) {
-            while (kq.valid && ik <= iv + 1) {
-                const int ks = ik % KSTAGES;
-                if (*sAbort || (ik >= KSTAGES && !mbar_wait_lazy(k_empty + 8 * ks, (ik / KSTAGES - 1) & 1))) {
-                    ok = false;
-                    break;
-                }
-                if (!(ik == p.stall_tile && blockIdx.x == 0))  // test hook: this window never lands
-                    load(kq, &tmk, s0 + (uint32_t)(OFF_K + ks * TILE), k_full + 8 * ks);
-                kq.next(p, it, lane);
-                ++ik;
-            }
-            if (!ok) break;
-            const int vs = iv & 1;
-            if (*sAbort || (iv >= VSTAGES && !mbar_wait_lazy(v_empty + 8 * vs, ((iv >> 1) - 1) & 1))) {
+        while (kq.valid) {
+            const int ks = ik % nst;
+            if (*sAbort || (ik >= nst && !mbar_wait_lazy(emptyb + 8 * ks, (ik / nst - 1) & 1))) {
                 ok = false;
                 break;
             }
-            load(vq, &tmv, s0 + (uint32_t)(OFF_V + vs * TILE), v_full + 8 * vs);
-            vq.next(p, it, lane);
-            ++iv;
+            cp_async_wait<BT_AHEAD - 1>();
+            const int z = coord(kq, ik);
+            prefetch(la, ik + BT_AHEAD);
+            if (la.valid) la.next(p, it, lane);
+            if (!(is_k && ik == p.stall_tile && blockIdx.x == 0))  // test hook: this K window never lands
+                load(map, ring + (uint32_t)(ks * TILE), fullb + 8 * ks, z);
+            kq.next(p, it, lane);
+            ++ik;
         }
+        cp_async_wait<0>();
         if (!ok) {
             if (lane == 0) {
                 *sAbort = 1;
                 atomicOr(p.header + 3, 1);
             }
             // the windows already requested land before the CTA can exit (bounded waits)
-            for (int j = ik > KSTAGES ? ik - KSTAGES : 0; j < ik; ++j)
-                mbar_wait(k_full + 8 * (j % KSTAGES), (j / KSTAGES) & 1);
-            for (int j = iv > VSTAGES ? iv - VSTAGES : 0; j < iv; ++j)
-                mbar_wait(v_full + 8 * (j & 1), (j >> 1) & 1);
+            for (int j = ik > nst ? ik - nst : 0; j < ik; ++j)
+                if (!(is_k && j == p.stall_tile && blockIdx.x == 0)) mbar_wait(fullb + 8 * (j % nst), (j / nst) & 1);
         }
     } else if (wid == WARP_MMA) {
         // ================================ MMA ================================
