@@ -25,6 +25,8 @@ q + out + cos/sin + tables), and microseconds per layer-step.
   config 3's long context split by KV chunk with the partials exchanged over peer memory
   (dvattn_lse_merge_peers; the NCCL all-gather path timed beside it), each with its
   efficiency against the same work on one GPU.
+* prefill_config4 (default workload): config 4 on the tensor-core prefill kernel, TFLOP/s
+  of whole calls and of the kernel alone against the measured bf16 peak.
 * Multi-GPU (torchrun): value is weak scaling -- every rank decodes its own batch of the
   same shape, no collective on the data path; value = all ranks' bytes / max-over-ranks
   time.  --workload long3: config 3 KV-chunk-sharded alone, one JSON line.
@@ -604,7 +606,8 @@ def run_ours(args, world, rank, local):
         # the same collective calls on every rank, so a failure is seen by all of them)
         for key, fn in (("config2_batch", (lambda: batch_strong_scaling(case, world, rank, args.steps))
                          if world > 1 else None),
-                        ("long3", lambda: long3_scaling(world, rank, dev, args.steps))):
+                        ("long3", lambda: long3_scaling(world, rank, dev, args.steps)),
+                        ("prefill_config4", lambda: prefill_leg(dev, 10, 3, world))):
             if fn is None:
                 continue
             try:
@@ -650,9 +653,64 @@ def run_ours(args, world, rank, local):
             "clocks": clocks,
             "cpu_baseline": cpu,
         }
+        if "prefill_config4" in extra:
+            line["prefill_config4"] = extra.pop("prefill_config4")
         if extra:
             line["strong_scaling"] = extra
         print(json.dumps(line), flush=True)
+
+
+def prefill_leg(dev, steps, warmup, world):
+    """Config 4 (bf16 varlen chunked prefill on the tcgen05 prefill_kernel) as an extra key of
+    the default line: whole calls over the C ABI back to back with three rotating KV pools
+    (inputs resident), and the attention kernel alone between events; TFLOP/s of the
+    attended q.k and p.v products, max over ranks, each rank its own batch."""
+    from dvattn_b200 import capi
+    from dvattn_b200 import workloads as wl
+    _, tf_peak, peak_kind = load_peaks()
+    case = wl.config4(device=dev)
+    flops = wl.varlen_flops(case)
+    out = case.new_out()
+    pools = [(case.k_cache, case.v_cache)]
+    for _ in range(2):
+        pools.append((torch.randn_like(case.k_cache, dtype=torch.float32).to(case.dtype),
+                      torch.randn_like(case.v_cache, dtype=torch.float32).to(case.dtype)))
+    calls, ws = [], None
+    for kc, vc in pools:
+        a = list(case.capi_args(out))
+        a[7], a[8] = kc, vc
+        call = capi.VarlenCall(*a, workspace=ws)
+        ws = call.workspace
+        calls.append(call)
+    stream = torch.cuda.current_stream()
+    for i in range(warmup):
+        calls[i % 3]()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        calls[i % 3]()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t_ms = max_over_ranks(e0.elapsed_time(e1), world) / steps
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        c = calls[i % 3]
+        c.phase(capi.DVATTN_PHASE_SCHEDULE)
+        kev[i][0].record(stream)
+        c.phase(capi.DVATTN_PHASE_ATTEND)
+        kev[i][1].record(stream)
+        c.phase(capi.DVATTN_PHASE_MERGE)
+    torch.cuda.synchronize()
+    k_ms = max_over_ranks(statistics.mean(x.elapsed_time(y) for x, y in kev), world)
+    achieved = flops / (k_ms * 1e-3) / 1e12
+    del pools, calls
+    return {"workload": "config4: bf16 varlen chunked prefill, 16 seqs, 32/2 heads, E=128, R=32, page 16",
+            "value": round(sum_over_ranks(float(flops), world) / (t_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "us_per_step": round(t_ms * 1e3, 1), "kernel": "prefill_kernel", "kernel_us": round(k_ms * 1e3, 1),
+            "achieved": round(achieved, 1), "peak": tf_peak, "peak_kind": peak_kind,
+            "frac": round(achieved / tf_peak, 4), "steps": steps, "scaling": "weak"}
 
 
 def run_varlen(args, world, rank, local):
