@@ -503,8 +503,10 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             if (first && !mbar_wait_lazy(q_ready, turn & 1)) { ok = false; break; }
             tc_fence_after();
             issue_s(0, ks);
+            // the softmax hand-offs (p_full) are polled without a pause: they are on every
+            // tile's critical path (softmax -> PV -> next S)
             if (i > 0) {
-                if (!mbar_wait_lazy(p_full + 8, (i - 1) & 1)) { ok = false; break; }
+                if (!mbar_wait(p_full + 8, (i - 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 issue_pv(1, vs ^ 1, i - 1 > 0);
                 commit(v_empty + 8 * (vs ^ 1));
@@ -514,7 +516,7 @@ __global__ void __launch_bounds__(NT, 1) prefill_kernel(Params p, const __grid_c
             issue_s(1, ks);
             commit(k_empty + 8 * ks);
             if (!mbar_wait_lazy(v_full + 8 * vs, (i >> 1) & 1)) { ok = false; break; }
-            if (!mbar_wait_lazy(p_full, i & 1)) { ok = false; break; }
+            if (!mbar_wait(p_full, i & 1)) { ok = false; break; }
             tc_fence_after();
             issue_pv(0, vs, i > 0);
             if (first) ++turn;
